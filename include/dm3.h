@@ -1,0 +1,150 @@
+/*
+ * drama3-b200 C ABI: the drop-in boundary for the Drama-3 per-frame MoE feed-forward and the
+ * block-FP8 GEMV, built for NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes raw device pointers, explicit sizes and strides, and a cudaStream_t
+ * passed as `void*` (0 = legacy default stream). Nothing here allocates device memory except
+ * where the caller hands in a workspace. All calls are asynchronous on the given stream and
+ * contain no host synchronisation (dm3_moe_status excepted), so they can be captured into CUDA
+ * graphs. The return value is DM3_OK or one of the DM3_E* codes below; dm3_last_error() gives a
+ * one-line reason.
+ *
+ * Dtypes: activations and outputs bf16 (uint16 storage), weights float8_e4m3fn (uint8 storage),
+ * scales fp32, expert ids int64, routing weights bf16.
+ *
+ * Scale layout ("srows"): an e4m3 weight [R, C] carries one fp32 scale per (srows x 128) block,
+ * stored row-major as [ceil(R / srows), C / 128]. srows = 128 is the 128x128 block layout of
+ * engine.fp8_block (engine.py:214-219, release/convert_weights.py:14-15); srows = 1 is the
+ * per-row 1x128 layout of fp8_linear.quantize (fp8_linear.py:30-34). Dequantised weight =
+ * float(q) * scale.
+ */
+#ifndef DM3_H
+#define DM3_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DM3_OK 0
+#define DM3_EINVAL 1   /* bad argument (shape, stride, alignment, null pointer) */
+#define DM3_ECUDA 2    /* a CUDA runtime call failed */
+#define DM3_ETIMEOUT 3 /* reported by dm3_moe_status: a device-side bounded wait ran out */
+#define DM3_ENOSPACE 4 /* workspace too small */
+
+/* Scale-table layouts accepted by every weight operand. */
+#define DM3_SCALE_1x128 1
+#define DM3_SCALE_128x128 128
+
+/* Router weight dtypes. */
+#define DM3_ROUTER_F32 0
+#define DM3_ROUTER_BF16 1
+
+/* One-line description of the last error on the calling host thread ("" if none). */
+const char* dm3_last_error(void);
+
+/* Library version, e.g. "0.1.0". */
+const char* dm3_version(void);
+
+/*
+ * Block-FP8 GEMV: y[m, n] = sum_k x[m, k] * float(q[n, k]) * s[n / srows, k / 128] (+ bias[n]),
+ * fp32 accumulation, for M <= 4 activation rows.
+ * Replaces the Triton `_gemv` kernel behind FP8Linear.forward for rows <= 2
+ * (fp8_linear.py:10-27, :56-59) and the restricted audio-head projection (engine.py:423).
+ *   x     bf16 [M, K], row stride K elements
+ *   q     e4m3 [N, K], row stride ldq bytes (ldq >= K, ldq % 16 == 0, 16-byte aligned base)
+ *   s     fp32 [ceil(N / srows), K / 128], row stride lds floats
+ *   bias  optional [N] (bias_kind 0 none, 1 bf16, 2 fp32)
+ *   y     [M, N] row stride ldy elements; y_fp32 = 0 writes bf16, 1 writes fp32
+ * K % 128 == 0, K <= 8192, 1 <= M <= 4.
+ */
+int dm3_fp8_gemv(const void* x, int M, int K, int N, const void* q, int64_t ldq, const float* s, int64_t lds,
+                 int srows, const void* bias, int bias_kind, void* y, int64_t ldy, int y_fp32, void* stream);
+
+/*
+ * Gathered block-FP8 GEMV: as dm3_fp8_gemv, but output row n reads weight row rows[n] of q
+ * (and its scale row rows[n] / srows). Covers the audio head restricted to the eos token plus
+ * the semantic band, `lm_head.weight[candidates]` (engine.py:409-411), without materialising
+ * the gathered copy. rows: int64 [N] on the device, each in [0, n_rows_q).
+ */
+int dm3_fp8_gemv_gather(const void* x, int M, int K, int N, const void* q, int64_t ldq, int64_t n_rows_q,
+                        const int64_t* rows, const float* s, int64_t lds, int srows, void* y, int64_t ldy,
+                        int y_fp32, void* stream);
+
+/*
+ * Workspace bytes needed by dm3_moe_forward / dm3_moe_layer for hidden H and expert intermediate
+ * I (sized for the maximum of 4 rows, so T is ignored). The workspace must be zero-filled once
+ * before its first use; every call leaves its counters at zero again, so it can be reused by
+ * later calls on the same stream (calls that overlap on the GPU must not share one workspace).
+ */
+size_t dm3_moe_workspace_bytes(int T, int H, int I);
+
+/*
+ * Grouped SwiGLU over block-FP8 experts with routing given by the caller:
+ *   y[t] = sum_j weights[t, j] * W2[e] ( silu(W1[e] x[t]) * W3[e] x[t] ),  e = ids[t, j]
+ * where W13[e] = [gate (rows 0..I-1); up (rows I..2I-1)] is [2I, H] e4m3 and W2[e] is [H, I]
+ * e4m3, each with its block scales; the SwiGLU activation is rounded to bf16 before the down
+ * projection and y is written as bf16. Replaces fish-speech `fp8_moe_forward(x, ids, w, w13,
+ * s13, w2, s2)` as called by OnDemandExperts.forward (engine.py:147) and Speaker.__call__
+ * (engine.py:236). This fused decode kernel covers T <= 4 rows.
+ *   x        bf16 [T, H]
+ *   ids      int64 [T, top_k] expert indices into dim 0 of w13/w2 (an ExpertStore slot or a
+ *            speaker expert); an id outside [0, n_experts) is skipped and flagged in the status
+ *   weights  bf16 [T, top_k]
+ *   w13      e4m3, expert e at w13 + e * w13_stride bytes, rows of H bytes
+ *   s13      fp32, expert e at s13 + e * s13_stride floats, layout [2I / srows, H / 128]
+ *   w2       e4m3, expert e at w2 + e * w2_stride bytes, rows of I bytes
+ *   s2       fp32, expert e at s2 + e * s2_stride floats, layout [H / srows, I / 128]
+ * ExpertStore slots (engine.py:32-34) have w13_stride = w2_stride = 3 * I * H.
+ * H % 128 == 0, H <= 2048, I % 128 == 0, I <= 512, top_k <= 8.
+ */
+int dm3_moe_forward(const void* x, int T, int H, int I, const int64_t* ids, const void* weights, int top_k,
+                    int n_experts, const void* w13, int64_t w13_stride, const float* s13, int64_t s13_stride,
+                    const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride, int srows, void* y,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Fused decode MoE layer in one launch: router + top-k + grouped SwiGLU + shared expert +
+ * combine. Covers Speaker.__call__ (engine.py:232-237: fp32 router over the distilled experts,
+ * softmax, top-k, renormalise, bf16 weights, fp8_moe_forward, + bias) and speaker_forward
+ * (engine.py:153-158: + sigmoid(shared_expert_gate(x)) * shared_expert(x)), and the same
+ * block with the full bf16 router (the routed SparseMoeBlock decode row).
+ *   router_w      [n_router, H], fp32 (router_dtype DM3_ROUTER_F32) or bf16
+ *   logits_bf16   1: logits are rounded to bf16 before softmax (a bf16 nn.Linear router);
+ *                 0: fp32 logits (the speaker's x.float() @ gate.T)
+ *   logit_bias    optional fp32 [n_router] added to the logits before softmax
+ *   experts       as dm3_moe_forward, n_experts = n_router
+ *   sh_w13/sh_s13/sh_w2/sh_s2  optional shared expert (null sh_w13 = none), e4m3 with scale
+ *                 layout sh_srows; sh_gate optional bf16 [H] (null: gate coefficient 1)
+ *   out_bias      optional fp32 [H] added before the final bf16 rounding (the speaker bias)
+ *   ids_out       optional int64 [T, top_k]: chosen experts, descending probability
+ *   w_out         optional bf16 [T, top_k]: renormalised routing weights
+ * Logits are accumulated exactly (fp64) and rounded once, so the chosen experts do not depend
+ * on summation order; ties are broken towards the lower expert index.
+ * n_router <= 256, top_k <= 8, T * top_k <= 32, other limits as dm3_moe_forward.
+ */
+int dm3_moe_layer(const void* x, int T, int H, int I, const void* router_w, int router_dtype, int n_router,
+                  int top_k, int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
+                  const float* s13, int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2,
+                  int64_t s2_stride, int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2,
+                  const float* sh_s2, int sh_srows, const void* sh_gate, const float* out_bias, void* y,
+                  int64_t* ids_out, void* w_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Reads and clears the sticky device status word of a MoE workspace (synchronises the
+ * stream). *status receives the STATUS bits (0 = every bounded wait completed and every
+ * expert id was valid; bit 0 = a wait timed out; bit 1 = an expert id was out of range).
+ * Returns DM3_ETIMEOUT if a wait ran out, DM3_OK otherwise.
+ */
+int dm3_moe_status(void* workspace, uint32_t* status, void* stream);
+
+/* Number of kernels the last MoE / GEMV entry point launched on this host thread. */
+int dm3_last_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DM3_H */
