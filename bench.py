@@ -1,0 +1,420 @@
+#!/usr/bin/env python
+"""Benchmark of the Drama-3 decode MoE feed-forward on B200.
+
+Default workload (`--workload decode`): 40 stacked MoE decode layers of the Drama-3 backbone
+shape (hidden 2048, 256 routed block-FP8 experts of intermediate 512 with 128x128 fp32 scales,
+top-8 softmax routing by a bf16 router, and an always-on block-FP8 shared expert behind a sigmoid
+gate). Each layer has independently seeded weights (N(0, 0.02)) and its own seeded 2-row input
+(conditional + unconditional guidance rows, N(0, 1) RMS-normalised, bf16). One step = one frame =
+the 40 layers, captured once in a CUDA graph and replayed. Weights total 30 GiB, far above the
+126 MB L2, so every replay streams them from HBM (no flush needed).
+
+Prints one JSON line: `value` = layer-frames per second over all ranks (device time, CUDA events,
+max over ranks), `us_per_layer`, the roofline of the fused MoE kernel against the measured HBM
+copy bandwidth, the CPU baseline (the reference's torch path on host cores), the end-to-end
+number through the public op with host buffers, and SM clocks sampled during the timed region.
+
+`--impl reference` times the reference's CPU implementation of the same layer (torch fp32 on all
+host cores) with the same metric. Other workloads: `--workload speaker` (40 distilled-speaker
+layers, 32 experts, fp32 router, bias) and `--workload gemv` (block-FP8 GEMV sweep).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+H, I, E, TOPK, T = 2048, 512, 256, 8, 2
+EXPERT_BYTES = 2 * I * H + H * I + (2 * I // 128) * (H // 128) * 4 + (H // 128) * (I // 128) * 4  # 3,146,496
+METRIC = "MoE decode layer throughput (2-row frame x layer / s); us/layer = 1e6 / (value / n_gpus)"
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def recorded_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get(kernel)
+    return None
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.out = ""
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        rows = [r.split(", ") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        loaded = [v for v in sm if v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- workload
+def rms(x):
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+
+
+def make_layer(seed: int, dev, experts=E, router_dtype=torch.bfloat16, shared=True, bias=False):
+    import drama3_b200 as dm3
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    L = {"gate": (torch.randn(experts, H, generator=g, device=dev) * 0.02).to(router_dtype)}
+    L["w13"], L["s13"] = dm3.fp8_block(torch.randn(experts, 2 * I, H, generator=g, device=dev) * 0.02)
+    L["w2"], L["s2"] = dm3.fp8_block(torch.randn(experts, H, I, generator=g, device=dev) * 0.02)
+    if shared:
+        L["sh_w13"], L["sh_s13"] = dm3.fp8_block(torch.randn(2 * I, H, generator=g, device=dev) * 0.02)
+        L["sh_w2"], L["sh_s2"] = dm3.fp8_block(torch.randn(H, I, generator=g, device=dev) * 0.02)
+        L["sh_gate"] = (torch.randn(H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    if bias:
+        L["bias"] = torch.randn(H, generator=g, device=dev) * 0.02
+    L["x"] = rms(torch.randn(T, H, generator=g, device=dev)).to(torch.bfloat16)
+    return L
+
+
+def layer_call(L, x, logits_bf16=True):
+    import drama3_b200 as dm3
+
+    return dm3.ops.moe_layer(x, L["gate"], TOPK, logits_bf16, None, L["w13"], L["s13"], L["w2"], L["s2"],
+                             L.get("sh_w13"), L.get("sh_s13"), L.get("sh_w2"), L.get("sh_s2"), L.get("sh_gate"),
+                             L.get("bias"))
+
+
+def layer_bytes(L, ids: torch.Tensor) -> int:
+    """Algorithmic HBM bytes of one layer: each distinct routed expert once (weights + scales),
+    the router, the shared expert and its gate row, the bias, and the activations in and out."""
+    u = int(torch.unique(ids).numel())
+    b = u * EXPERT_BYTES + L["gate"].numel() * L["gate"].element_size() + 2 * T * H * 2
+    if "sh_w13" in L:
+        b += EXPERT_BYTES + H * 2
+    if "bias" in L:
+        b += H * 4
+    return b
+
+
+def cpu_layer(L) -> dict:
+    return {k: v.cpu() for k, v in L.items()}
+
+
+def time_cpu_port(layers_cpu, budget_s: float):
+    """Times oracle.cpu_port.decode_layer on host cores; returns (layer-frames/s, reps, threads)."""
+    from oracle import cpu_port
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_port.decode_layer(layers_cpu[0]["x"], layers_cpu[0])  # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        L = layers_cpu[reps % len(layers_cpu)]
+        cpu_port.decode_layer(L["x"], L)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 200:
+            break
+    return reps / el, reps, torch.get_num_threads()
+
+
+def run_decode(args, world, rank, local, speaker=False):
+    import drama3_b200 as dm3
+
+    dev = torch.device("cuda", local)
+    n_layers = args.layers
+    kw = dict(experts=32, router_dtype=torch.float32, shared=True, bias=True) if speaker else {}
+    layers = [make_layer(1000 * (rank + 1) + l, dev, **kw) for l in range(n_layers)]
+    torch.cuda.synchronize()
+    logits_bf16 = not speaker
+    outs = [layer_call(L, L["x"], logits_bf16) for L in layers]  # eager warm-up (creates the workspace)
+    torch.cuda.synchronize()
+    bytes_step = sum(layer_bytes(L, o[1]) for L, o in zip(layers, outs))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gouts = [layer_call(L, L["x"], logits_bf16) for L in layers]
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    ws = dm3.ops.moe_workspace(dev, H, I)
+    assert dm3.ops.moe_status(ws) == 0, "device status word set during warm-up"
+    for o, g in zip(outs, gouts):
+        assert torch.equal(o[1], g[1]), "graph replay routed differently from eager"
+
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    launches = args.steps * n_layers
+
+    # end to end through the public op with host buffers: every layer's rows H2D from pinned memory
+    # (one copy), the captured frame, and the frame's result (the last layer's rows) D2H
+    xs_host = torch.stack([L["x"].cpu() for L in layers]).pin_memory()
+    y_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xs_dev = torch.stack([L["x"] for L in layers])
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        g2outs = [layer_call(L, xs_dev[l], logits_bf16)[0] for l, L in enumerate(layers)]
+
+    def e2e_step():
+        xs_dev.copy_(xs_host, non_blocking=True)
+        g2.replay()
+        y_host.copy_(g2outs[-1], non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+
+    pk = peaks()
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    value = world * n_layers * 1000.0 / ms
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "layer-frames/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "us_per_layer": round(ms * 1000.0 / n_layers, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, RMS-normalised N(0,1) rows)",
+        "config": {
+            "workload": ("speaker_decode_fp8_32x40" if speaker else "decode_fp8_256x40"),
+            "layers": n_layers, "rows": T, "hidden": H, "intermediate": I,
+            "experts": 32 if speaker else E, "top_k": TOPK,
+            "router": "fp32 (speaker)" if speaker else "bf16, logits rounded to bf16",
+            "shared_expert": "block-FP8 128x128 + bf16 sigmoid gate",
+            "scales": "128x128 fp32", "cuda_graph": True,
+            "l2": "no flush: 40 layers stream > 2 GB of weights per step (L2 126 MB)",
+            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": pk["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": round(achieved / pk["hbm_gbs"], 4),
+            "peak_source": f"{pk['source']} HBM copy bandwidth",
+            "kernel": "dm3::moe::moe_decode_kernel",
+            "bytes_per_launch": round(bytes_step / n_layers),
+            "traffic": recorded_traffic("moe_decode_kernel"),
+        },
+        "gpu_launches": launches,
+        "e2e": {
+            "value": round(world * n_layers * 1000.0 / ms_e2e, 1),
+            "unit": "layer-frames/s",
+            "h2d_bytes_per_step": int(xs_host.numel() * 2),
+            "d2h_bytes_per_step": int(y_host.numel() * 2),
+            "ms_per_step": round(ms_e2e, 4),
+            "path": "pinned host rows -> H2D -> captured drama3_b200.ops.moe_layer x 40 -> D2H of the last layer",
+        },
+    }
+    clk_sum = clk.summary()
+    line["clocks"] = {k: clk_sum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu_layers = [cpu_layer(L) for L in layers[:2]]
+        v, reps, thr = time_cpu_port(cpu_layers, budget_s=args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(v, 3), "unit": "layer-frames/s", "cores": thr, "kind": "port",
+                                "sample": f"{reps} layer evaluations of the same workload (2 layers cycled), torch fp32 "
+                                          "on host cores (oracle/cpu_port.py)"}
+    return line
+
+
+def run_gemv(args, world, rank, local):
+    """Block-FP8 GEMV sweep: per shape, 40 distinct weight copies in one graph (each launch reads
+    cold weights, as the reference's own timing rotates 40 layers, fp8_linear.py:82-103)."""
+    import drama3_b200 as dm3
+
+    dev = torch.device("cuda", local)
+    res = {}
+    copies = 40
+    for (k, n) in [(2048, 4096), (4096, 2048), (2048, 8192), (2048, 512), (2048, 4097)]:
+        g = torch.Generator(device=dev).manual_seed(k + n)
+        ws = [dm3.quantize(torch.randn(n, k, generator=g, device=dev) * 0.02) for _ in range(copies)]
+        x = rms(torch.randn(2, k, generator=g, device=dev)).to(torch.bfloat16)
+        [dm3.ops.fp8_gemv(x, q, s) for q, s in ws]
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ys = [dm3.ops.fp8_gemv(x, q, s) for q, s in ws]
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (args.steps * copies)
+        nbytes = n * k + n * (k // 128) * 4 + 2 * k * 2 + 2 * n * 2
+        res[f"{k}x{n}"] = {"us": round(us, 3), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
+                           "frac": round(nbytes / (us * 1e-6) / 1e9 / peaks()["hbm_gbs"], 4)}
+        del ws, ys, graph
+    main_key = "2048x4096"
+    return {"metric": "block-FP8 GEMV (M=2) per call", "value": res[main_key]["us"], "unit": "us/call",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x bf16", "data": "synthetic",
+            "config": {"workload": "gemv_sweep_m2_1x128", "copies": copies}, "shapes": res,
+            "gpu_launches": args.steps * copies}
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU path for the decode layer (torch fp32 on host cores), same metric."""
+    if rank != 0:
+        return None
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    layers = [cpu_layer(make_layer(1000 + l, dev)) for l in range(2)]
+    from oracle import cpu_port
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    for i in range(max(args.warmup, 1)):
+        L = layers[i % 2]
+        cpu_port.decode_layer(L["x"], L)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        L = layers[i % 2]
+        cpu_port.decode_layer(L["x"], L)
+    el = time.perf_counter() - t0
+    v = args.steps / el
+    thr = torch.get_num_threads()
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "layer-frames/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el * 1000 / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (CPU)",
+            "data": "synthetic", "config": {"workload": "decode_fp8_256x40", "rows": T, "hidden": H,
+                                            "intermediate": I, "experts": E, "top_k": TOPK,
+                                            "sample": "one layer per step, 2 layers cycled"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "layer-frames/s", "cores": thr, "kind": "port",
+                             "sample": f"{args.steps} layer evaluations, torch fp32 on {thr} host threads"},
+            "e2e": {"value": round(v, 3), "unit": "layer-frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "speaker", "gemv"])
+    ap.add_argument("--layers", type=int, default=40)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, world, rank)
+        elif args.workload == "gemv":
+            line = run_gemv(args, world, rank, local)
+        else:
+            line = run_decode(args, world, rank, local, speaker=args.workload == "speaker")
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
