@@ -32,6 +32,8 @@ SIGNATURES = {
     "dm3_moe_layer": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p,
                            _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _sz, _p]),
     "dm3_moe_status": (_i, [_p, _u32p, _p]),
+    "dm3_moe_layer_noalloc": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i,
+                                   _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p]),
     "dm3_last_launch_count": (_i, []),
 }
 

@@ -1170,3 +1170,46 @@ extern "C" int dm3_moe_status(void* workspace, uint32_t* status, void* stream) {
   *status = v;
   return (v & dm3::STATUS_TIMEOUT) ? 3 : 0;
 }
+
+// ------------------------------------------------------------------ allocation-free variant
+// For callers that cannot allocate device memory at all: a caller running inside another
+// runtime's memory pool, a plugin host that hands out only its own buffers, or code on a path
+// where cudaMalloc is forbidden (it may synchronise the device and is not allowed during stream
+// capture). The fused layer's scratch then lives in this file-scope device array instead of a
+// caller-provided workspace. Every GPU that loads the library reserves it until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 1310720;  // 1.25 MiB: the workspace of H <= 2048, I <= 512
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+// Device address of g_noalloc_scratch per device; the host-side symbol is not a device address.
+void* g_noalloc_ptr[64] = {nullptr};
+
+}  // namespace
+
+extern "C" int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const void* router_w, int router_dtype,
+                                     int n_router, int top_k, int logits_bf16, const float* logit_bias,
+                                     const void* w13, int64_t w13_stride, const float* s13, int64_t s13_stride,
+                                     const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride, int srows,
+                                     const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
+                                     int sh_srows, const void* sh_gate, const float* out_bias, void* y,
+                                     int64_t* ids_out, void* w_out, void* stream) {
+  dm3::note_launches(0);
+  if (H > 0 && I > 0 && H <= dm3::kMaxH && I <= dm3::kMaxI &&
+      dm3::moe_ws_bytes(dm3::kMaxT, H, I) > kNoAllocScratchBytes)
+    return dm3::set_error("H and I need more scratch than the 1.25 MiB static array holds"), 4;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return dm3::set_error("no usable current CUDA device"), 2;
+  if (g_noalloc_ptr[dev] == nullptr) {
+    // first call on this device: look up the array's device address and zero it once
+    void* ptr = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess) return dm3::set_error(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(err)), 2;
+    err = cudaMemsetAsync(ptr, 0, kNoAllocScratchBytes, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return dm3::set_error(std::string("clearing the static scratch: ") + cudaGetErrorString(err)), 2;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  return dm3_moe_layer(x, T, H, I, router_w, router_dtype, n_router, top_k, logits_bf16, logit_bias, w13, w13_stride,
+                       s13, s13_stride, w2, w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows,
+                       sh_gate, out_bias, y, ids_out, w_out, g_noalloc_ptr[dev], kNoAllocScratchBytes, stream);
+}

@@ -140,6 +140,25 @@ int dm3_moe_layer(const void* x, int T, int H, int I, const void* router_w, int 
  */
 int dm3_moe_status(void* workspace, uint32_t* status, void* stream);
 
+/*
+ * dm3_moe_layer without a workspace argument, for callers that cannot allocate device memory:
+ * code running inside another runtime's memory pool, plugin hosts that only hand out their own
+ * buffers, or paths where cudaMalloc is not allowed. It has no counterpart in the reference.
+ * Arguments and results are those of dm3_moe_layer. The scratch is a 1.25 MiB array compiled
+ * into the library, held by every GPU that loads it until the process exits; H <= 2048 and
+ * I <= 512 always fit, and sizes beyond the array are rejected with DM3_ENOSPACE. The first
+ * call on a device looks up the array's address and zeroes it on the given stream, so make
+ * that first call before any stream capture. All calls share the one array and each call leaves
+ * it ready for the next, so calls that overlap on the GPU race; the device status word of this
+ * scratch is not reported. Allocates nothing.
+ */
+int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const void* router_w, int router_dtype, int n_router,
+                          int top_k, int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
+                          const float* s13, int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2,
+                          int64_t s2_stride, int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2,
+                          const float* sh_s2, int sh_srows, const void* sh_gate, const float* out_bias, void* y,
+                          int64_t* ids_out, void* w_out, void* stream);
+
 /* Number of kernels the last MoE / GEMV entry point launched on this host thread. */
 int dm3_last_launch_count(void);
 
