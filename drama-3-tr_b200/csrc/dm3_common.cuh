@@ -125,40 +125,61 @@ __device__ __forceinline__ void named_bar(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// ---------------------------------------------------------------- shared-memory vector load
-__device__ __forceinline__ uint4 lds128(const void* p) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(smem_u32(p)));
-  return v;
-}
-
 // ---------------------------------------------------------------- FP8 tensor-core tile
 // D[16x8] += A[16x32] (e4m3, row) * B[32x8] (e4m3, col), fp32 accumulate.
 // Lane (g = lane/4, q = lane%4) holds A rows g and g+8 at k = {4q..4q+3, 16+4q..16+4q+3},
 // B column g at the same k, and C rows g, g+8 at columns 2q, 2q+1.
+// Not volatile: a pure function of its operands, so the compiler may schedule independent MMAs
+// back to back.
 __device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Multiplies a 16-row weight tile (two smem rows per lane: row_lo = tile row g, row_hi = g+8)
-// by the 8 split-activation columns over 64 k starting at byte offset `off` of each row.
-// Each lane reads 16 contiguous bytes of its two rows and of its B column, which fixes the
-// k <-> fragment-slot permutation identically for A and B.
-__device__ __forceinline__ void mma_k64(float (&acc)[4], const uint8_t* row_lo, const uint8_t* row_hi,
-                                        const uint8_t* bcol, bool bvalid, int off) {
-  const uint4 a = lds128(row_lo + off);
-  const uint4 c = lds128(row_hi + off);
-  uint4 b = make_uint4(0u, 0u, 0u, 0u);
-  if (bvalid) b = lds128(bcol + off);
-  mma_e4m3(acc, a.x, c.x, a.y, c.y, b.x, b.y);
-  mma_e4m3(acc, a.z, c.z, a.w, c.w, b.z, b.w);
+__device__ __forceinline__ uint4 ld_smem16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Raw products of a 16-row e4m3 tile (smem rows row_lo = tile row g, row_hi = g + 8) and the 8
+// split-activation B columns (bcol = column g) over the 128-wide k blocks kbs[0..NK): out[i][.] is
+// the fp32 partial of k block kbs[i] (C fragment layout). Every fragment is loaded before the first
+// MMA and each 32-wide k step has its own accumulator, so the loads and the 4 * NK MMAs overlap.
+// Each lane reads 16 contiguous bytes of its rows and its B column per 64 k, which fixes the same
+// k <-> fragment-slot permutation for A and B.
+template <int NK>
+__device__ __forceinline__ void tile_kblocks(float (&out)[NK][4], const uint8_t* row_lo, const uint8_t* row_hi,
+                                             const uint8_t* bcol, bool lo_ok, bool hi_ok, bool bvalid,
+                                             const int (&kbs)[NK], int q) {
+  uint4 a[NK][2], c[NK][2], b[NK][2];
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+  for (int i = 0; i < NK; ++i)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int off = kbs[i] * 128 + 64 * j + 16 * q;
+      a[i][j] = lo_ok ? ld_smem16(row_lo + off) : z;
+      c[i][j] = hi_ok ? ld_smem16(row_hi + off) : z;
+      b[i][j] = bvalid ? ld_smem16(bcol + off) : z;
+    }
+  float t[NK][4][4];
+#pragma unroll
+  for (int i = 0; i < NK; ++i)
+#pragma unroll
+    for (int h = 0; h < 4; ++h)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) t[i][h][e] = 0.f;
+#pragma unroll
+  for (int i = 0; i < NK; ++i)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      mma_e4m3(t[i][2 * j], a[i][j].x, c[i][j].x, a[i][j].y, c[i][j].y, b[i][j].x, b[i][j].y);
+      mma_e4m3(t[i][2 * j + 1], a[i][j].z, c[i][j].z, a[i][j].w, c[i][j].w, b[i][j].z, b[i][j].w);
+    }
+#pragma unroll
+  for (int i = 0; i < NK; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) out[i][e] = (t[i][0][e] + t[i][1][e]) + (t[i][2][e] + t[i][3][e]);
 }
 
 // ---------------------------------------------------------------- exact bf16 -> e4m3 hi/lo split

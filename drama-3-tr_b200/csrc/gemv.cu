@@ -79,17 +79,6 @@ __device__ __forceinline__ int64_t src_row(const Params& p, int r) {
   return v;
 }
 
-__device__ __forceinline__ void mma_k64_rows(float (&acc)[4], const uint8_t* row_lo, bool lo_ok,
-                                             const uint8_t* row_hi, bool hi_ok, const uint8_t* bcol, bool bvalid,
-                                             int off) {
-  uint4 a = make_uint4(0u, 0u, 0u, 0u), c = a, b = a;
-  if (lo_ok) a = lds128(row_lo + off);
-  if (hi_ok) c = lds128(row_hi + off);
-  if (bvalid) b = lds128(bcol + off);
-  mma_e4m3(acc, a.x, c.x, a.y, c.y, b.x, b.y);
-  mma_e4m3(acc, a.z, c.z, a.w, c.w, b.z, b.w);
-}
-
 __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Smem S = smem_layout(p.K, p.tile_rows);
@@ -213,23 +202,30 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
       const float* gs_lo = p.s + (lo_ok ? (src_row(p, r0 + g) / p.srows) * p.lds : 0);
       const float* gs_hi = p.s + (hi_ok ? (src_row(p, r0 + g + 8) / p.srows) * p.lds : 0);
       float tot[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-      for (int kb = warp; kb < nkb; kb += kConsumerWarps) {
-        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-        mma_k64_rows(a0, row_lo, lo_ok, row_hi, hi_ok, bcol, bvalid, kb * 128 + 16 * q);
-        mma_k64_rows(a1, row_lo, lo_ok, row_hi, hi_ok, bcol, bvalid, kb * 128 + 64 + 16 * q);
-        float s0 = 0.f, s1 = 0.f;
-        if (p.sc_bulk) {
-          if (lo_ok) s0 = sc[si_lo * nkb + kb];
-          if (hi_ok) s1 = sc[si_hi * nkb + kb];
-        } else {
-          if (lo_ok) s0 = __ldg(gs_lo + kb);
-          if (hi_ok) s1 = __ldg(gs_hi + kb);
+      // this warp's k blocks: warp, warp + 8, ...; two per pass, all fragments loaded up front
+      for (int kb0 = warp; kb0 < nkb; kb0 += 2 * kConsumerWarps) {
+        const int kb1 = kb0 + kConsumerWarps;
+        const bool v1 = kb1 < nkb;
+        const int kbs[2] = {kb0, v1 ? kb1 : kb0};
+        float part[2][4];
+        tile_kblocks<2>(part, row_lo, row_hi, bcol, lo_ok, hi_ok, bvalid, kbs, q);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          float s0 = 0.f, s1 = 0.f;
+          if (i == 0 || v1) {
+            if (p.sc_bulk) {
+              if (lo_ok) s0 = sc[si_lo * nkb + kbs[i]];
+              if (hi_ok) s1 = sc[si_hi * nkb + kbs[i]];
+            } else {
+              if (lo_ok) s0 = __ldg(gs_lo + kbs[i]);
+              if (hi_ok) s1 = __ldg(gs_hi + kbs[i]);
+            }
+          }
+          tot[0] = fmaf(part[i][0], s0, tot[0]);
+          tot[1] = fmaf(part[i][1], s0, tot[1]);
+          tot[2] = fmaf(part[i][2], s1, tot[2]);
+          tot[3] = fmaf(part[i][3], s1, tot[3]);
         }
-        tot[0] = fmaf(a0[0] + a1[0], s0, tot[0]);
-        tot[1] = fmaf(a0[1] + a1[1], s0, tot[1]);
-        tot[2] = fmaf(a0[2] + a1[2], s1, tot[2]);
-        tot[3] = fmaf(a0[3] + a1[3], s1, tot[3]);
       }
 #pragma unroll
       for (int j = 0; j < 4; ++j) tot[j] += __shfl_down_sync(0xffffffffu, tot[j], 2);

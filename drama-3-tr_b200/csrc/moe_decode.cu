@@ -384,9 +384,10 @@ __device__ void consume_g(const Params& p, const WsLayout& L, const SmemLayout& 
   float tot[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
   for (int kb = gw; kb < nkb; kb += kGroupWarps) {
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_k64(a0, row_lo, row_hi, bcol, bvalid, kb * 128 + 16 * q);
-    mma_k64(a1, row_lo, row_hi, bcol, bvalid, kb * 128 + 64 + 16 * q);
+    float part[1][4];
+    const int kbs[1] = {kb};
+    tile_kblocks<1>(part, row_lo, row_hi, bcol, true, true, bvalid, kbs, q);
+    const float a0[4] = {part[0][0], part[0][1], part[0][2], part[0][3]}, a1[4] = {0.f, 0.f, 0.f, 0.f};
     float sgv, suv;
     if (ex.sc13_bulk) {
       sgv = sc[sg_row * nkb + kb];
@@ -496,9 +497,10 @@ __device__ void consume_d(const Params& p, const WsLayout& L, const SmemLayout& 
   float tot[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
   for (int kb = 0; kb < nkb; ++kb) {
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-    mma_k64(a0, row_lo, row_hi, bcol, bvalid, kb * 128 + 16 * q);
-    mma_k64(a1, row_lo, row_hi, bcol, bvalid, kb * 128 + 64 + 16 * q);
+    float part[1][4];
+    const int kbs[1] = {kb};
+    tile_kblocks<1>(part, row_lo, row_hi, bcol, true, true, bvalid, kbs, q);
+    const float a0[4] = {part[0][0], part[0][1], part[0][2], part[0][3]}, a1[4] = {0.f, 0.f, 0.f, 0.f};
     float s0, s1;
     if (ex.sc2_bulk) {
       s0 = sc[(ex.srows == 1 ? r_lo : 0) * nkb + kb];
