@@ -292,94 +292,91 @@ __device__ int load_table(const Params& p, const WsLayout& L, int lane, int* tab
 }
 
 // ------------------------------------------------------------------ route kernel
-// Top-k per row over the logits, renormalised weights and the slot table, by one warp. Mirrors
-// Speaker.__call__ (engine.py:233-235): probs = softmax(logits), (w, ids) = probs.topk(k),
+// Router logits in shared memory of the last route CTA: [kMaxT][kMaxRouter + 1] floats (the last
+// column is the shared expert's gate), then the selected experts and weights of every row.
+struct RouteSmem {
+  float logits[kMaxT][kMaxRouter + 1];
+  int sel_e[kMaxT * kMaxTopK];
+  float sel_w[kMaxT * kMaxTopK];
+  float shared_coef[kMaxT];
+  int last;
+};
+
+// Top-k of row t by one warp from the logits in shared memory, and the renormalised weights.
+// Mirrors Speaker.__call__ (engine.py:233-235): probs = softmax(logits), (w, ids) = probs.topk(k),
 // w = (w / w.sum()).to(bf16). Selection uses the logits themselves (softmax is monotonic), ties to
 // the lower index.
-__device__ void finalize_route(const Params& p, const WsLayout& L, int lane) {
-  const int T = p.T, E = p.n_router, K = p.top_k;
-  const float* logits = reinterpret_cast<const float*>(p.ws + L.logits);
-  int my_t = 0, my_e = -1;
-  float my_w = 0.f;
-  float shared_coef[kMaxT] = {1.f, 1.f, 1.f, 1.f};
-  for (int t = 0; t < T; ++t) {
-    float lv[kMaxRouter / 32];
-    float m = -FLT_MAX;
+__device__ void route_row(const Params& p, RouteSmem& rs, int t, int lane) {
+  const int E = p.n_router, K = p.top_k;
+  float lv[kMaxRouter / 32];
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < kMaxRouter / 32; ++i) {
+    const int e = lane + 32 * i;
+    lv[i] = e < E ? rs.logits[t][e] : -FLT_MAX;
+    m = fmaxf(m, lv[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float z = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxRouter / 32; ++i)
+    if (lane + 32 * i < E) z += expf(lv[i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  unsigned taken = 0u;
+  float psum = 0.f, my_p = 0.f;
+  int my_e = -1;
+  for (int j = 0; j < K; ++j) {
+    float bv = -FLT_MAX;
+    int be = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < kMaxRouter / 32; ++i) {
       const int e = lane + 32 * i;
-      lv[i] = e < E ? __ldcg(logits + t * (kMaxRouter + 1) + e) : -FLT_MAX;
-      m = fmaxf(m, lv[i]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float z = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxRouter / 32; ++i)
-      if (lane + 32 * i < E) z += expf(lv[i] - m);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-    unsigned taken = 0u;
-    float pj[kMaxTopK];
-    int ej[kMaxTopK];
-    for (int j = 0; j < K; ++j) {
-      float bv = -FLT_MAX;
-      int be = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < kMaxRouter / 32; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E && !(taken & (1u << i)) && (lv[i] > bv || (lv[i] == bv && e < be))) {
-          bv = lv[i];
-          be = e;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-        if (ov > bv || (ov == bv && oe < be)) {
-          bv = ov;
-          be = oe;
-        }
-      }
-      if ((be & 31) == lane) taken |= 1u << (be >> 5);
-      ej[j] = be;
-      pj[j] = expf(bv - m) / z;
-    }
-    float s = 0.f;
-    for (int j = 0; j < K; ++j) s += pj[j];
-    for (int j = 0; j < K; ++j) {
-      const __nv_bfloat16 wb = __float2bfloat16_rn(pj[j] / s);
-      if (lane == t * K + j) {
-        my_t = t;
-        my_e = ej[j];
-        my_w = __bfloat162float(wb);
-      }
-      if (lane == 0) {
-        if (p.ids_out) p.ids_out[t * K + j] = ej[j];
-        if (p.w_out) p.w_out[t * K + j] = wb;
+      if (e < E && !(taken & (1u << i)) && (lv[i] > bv || (lv[i] == bv && e < be))) {
+        bv = lv[i];
+        be = e;
       }
     }
-    if (p.sh_gate) {
-      const float gl = __ldcg(logits + t * (kMaxRouter + 1) + E);
-      shared_coef[t] = bf16_round(1.f / (1.f + expf(-gl)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+    const float pj = expf(bv - m) / z;
+    psum += pj;
+    if (lane == j) {
+      my_e = be;
+      my_p = pj;
     }
   }
-  int* slot_expert = reinterpret_cast<int*>(p.ws + L.slot_expert);
-  float* coef = reinterpret_cast<float*>(p.ws + L.coef);
-  const int n_slots = build_slots(lane, T * K, my_t, my_e, my_w, p.sh_w13 != nullptr, T, slot_expert, coef,
-                                  shared_coef);
-  if (lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(n_slots);
+  if (lane < K) {
+    const __nv_bfloat16 wb = __float2bfloat16_rn(my_p / psum);
+    rs.sel_e[t * K + lane] = my_e;
+    rs.sel_w[t * K + lane] = __bfloat162float(wb);
+    if (p.ids_out) p.ids_out[t * K + lane] = my_e;
+    if (p.w_out) p.w_out[t * K + lane] = wb;
+  }
+  if (lane == 0)
+    rs.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-rs.logits[t][E]))) : 1.f;
 }
 
 // One warp per router row (plus the shared expert's gate row). The row is fetched into registers
-// before griddepcontrol.wait (router weights never depend on the preceding kernel), then dotted
-// with every activation row exactly in fp64 (bf16 x bf16 and bf16 x fp32 products are exact in
-// fp64) and rounded once to fp32 (then to bf16 for a bf16 router), + the optional logit bias. The
-// shared gate row is rounded to bf16 as a bf16 linear's output. The last CTA to finish builds the
-// route table; its one gpu-scope fence runs with no copies in flight.
+// before griddepcontrol.wait (router weights never depend on the preceding kernel); the activation
+// rows are staged in shared memory after it, all loads in flight at once. Each logit is an exact
+// fp64 dot product (bf16 x bf16 and bf16 x fp32 products are exact in fp64) rounded once to fp32
+// (then to bf16 for a bf16 router), + the optional logit bias; the shared gate row is rounded to
+// bf16 as a bf16 linear's output. The last CTA to finish (one gpu-scope fence per CTA, with no
+// copies in flight) runs the top-k of every row in parallel and writes the slot table.
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p) {
   const WsLayout L = ws_layout(p.H, p.I);
+  __shared__ __align__(16) __nv_bfloat16 xs[kMaxT * kMaxH];
+  __shared__ RouteSmem rs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool sh_gate_row = p.sh_w13 != nullptr && p.sh_gate != nullptr;
   const int rows = p.n_router + (sh_gate_row ? 1 : 0);
@@ -397,16 +394,32 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p)
                                                                  static_cast<size_t>(row) * p.H)
                                  : reinterpret_cast<const uint4*>(p.sh_gate);
 #pragma unroll
-    for (int j = 0; j < kMaxChunks; ++j)
-      if (j < chunks) wv[j] = __ldg(src + lane + 32 * j);
+    for (int j = 0; j < kMaxChunks; ++j) wv[j] = j < chunks ? __ldg(src + lane + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
   }
   griddep_wait();
   griddep_launch();
+  {
+    constexpr int kPerThread = kMaxT * kMaxH / 8 / (kRouteWarps * 32);
+    const int n16 = p.T * p.H / 8;
+    const uint4* xsrc = reinterpret_cast<const uint4*>(p.x);
+    uint4 v[kPerThread];
+#pragma unroll
+    for (int i = 0; i < kPerThread; ++i) {
+      const int c = threadIdx.x + i * kRouteWarps * 32;
+      v[i] = c < n16 ? xsrc[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kPerThread; ++i) {
+      const int c = threadIdx.x + i * kRouteWarps * 32;
+      if (c < n16) reinterpret_cast<uint4*>(xs)[c] = v[i];
+    }
+  }
+  __syncthreads();
   float* logits = reinterpret_cast<float*>(p.ws + L.logits);
   if (row < rows) {
     for (int t = 0; t < p.T; ++t) {
-      const __nv_bfloat16* xr = p.x + static_cast<size_t>(t) * p.H;
-      double acc0 = 0.0, acc1 = 0.0;
+      const __nv_bfloat16* xr = xs + t * p.H;
+      double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
       for (int j = 0; j < kMaxChunks; ++j) {
         if (j < chunks) {
@@ -414,29 +427,25 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p)
             const float* w = reinterpret_cast<const float*>(&wv[j]);
             const uint2 xv = *reinterpret_cast<const uint2*>(xr + lane * 4 + 128 * j);
             const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-            acc0 = fma(static_cast<double>(__bfloat162float(xe[0])), static_cast<double>(w[0]), acc0);
-            acc1 = fma(static_cast<double>(__bfloat162float(xe[1])), static_cast<double>(w[1]), acc1);
-            acc0 = fma(static_cast<double>(__bfloat162float(xe[2])), static_cast<double>(w[2]), acc0);
-            acc1 = fma(static_cast<double>(__bfloat162float(xe[3])), static_cast<double>(w[3]), acc1);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              acc[i] = fma(static_cast<double>(__bfloat162float(xe[i])), static_cast<double>(w[i]), acc[i]);
           } else {
             const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
             const uint4 xv = *reinterpret_cast<const uint4*>(xr + lane * 8 + 256 * j);
             const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-              acc0 = fma(static_cast<double>(__bfloat162float(xe[i])), static_cast<double>(__bfloat162float(w[i])),
-                         acc0);
-              acc1 = fma(static_cast<double>(__bfloat162float(xe[i + 1])),
-                         static_cast<double>(__bfloat162float(w[i + 1])), acc1);
-            }
+            for (int i = 0; i < 8; ++i)
+              acc[i & 3] = fma(static_cast<double>(__bfloat162float(xe[i])),
+                               static_cast<double>(__bfloat162float(w[i])), acc[i & 3]);
           }
         }
       }
-      double acc = acc0 + acc1;
+      double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
       if (lane == 0) {
-        float v = __double2float_rn(acc);
+        float v = __double2float_rn(sum);
         if (is_router) {
           if (p.logits_bf16) v = bf16_round(v);
           if (p.logit_bias) v += p.logit_bias[row];
@@ -447,18 +456,37 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p)
       }
     }
   }
-  __shared__ int last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
     const uint32_t old = atomicAdd(ctrl(p, L) + CTRL_ROUTE_COUNT, 1u);
-    last = old == gridDim.x - 1;
-    if (last) __threadfence();
+    rs.last = old == gridDim.x - 1;
+    if (rs.last) __threadfence();
   }
   __syncthreads();
-  if (last && warp == 0) {
-    finalize_route(p, L, lane);
-    if (lane == 0) ctrl(p, L)[CTRL_ROUTE_COUNT] = 0u;  // every CTA has counted: ready for the next call
+  if (!rs.last) return;
+  // last CTA: every logit is visible; stage them, one warp per row for the top-k, then the table
+  for (int i = threadIdx.x; i < p.T * (kMaxRouter + 1); i += kRouteWarps * 32) {
+    const int t = i / (kMaxRouter + 1), e = i % (kMaxRouter + 1);
+    rs.logits[t][e] = e < rows ? __ldcg(logits + i) : 0.f;
+  }
+  __syncthreads();
+  if (warp < p.T) route_row(p, rs, warp, lane);
+  __syncthreads();
+  if (warp == 0) {
+    const int K = p.top_k;
+    const int n = p.T * K;
+    const int my_t = lane < n ? lane / K : 0;
+    const int my_e = lane < n ? rs.sel_e[lane] : -1;
+    const float my_w = lane < n ? rs.sel_w[lane] : 0.f;
+    int* slot_expert = reinterpret_cast<int*>(p.ws + L.slot_expert);
+    float* coef = reinterpret_cast<float*>(p.ws + L.coef);
+    const int n_slots = build_slots(lane, n, my_t, my_e, my_w, p.sh_w13 != nullptr, p.T, slot_expert, coef,
+                                    rs.shared_coef);
+    if (lane == 0) {
+      ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(n_slots);
+      ctrl(p, L)[CTRL_ROUTE_COUNT] = 0u;  // every CTA has counted: ready for the next call
+    }
   }
 }
 
@@ -701,6 +729,9 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const Params p) {
     auto get_table = [&]() {
       n_slots = load_table(p, L, lane, tab_expert, tab_coef, !DOWN);
       have_table = true;
+      // with routing given, the up kernel publishes the slot count for the combine kernel (after its
+      // wait, so the previous call's combine has finished reading it)
+      if (!DOWN && p.mode == 0 && blockIdx.x == 0 && lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(n_slots);
     };
     auto wait_predecessor = [&]() {
       griddep_wait();
@@ -834,10 +865,6 @@ __global__ void __launch_bounds__(kThreads, 1) expert_kernel(const Params p) {
 // speaker_forward's bf16 tensor sum (engine.py:158). One thread per output element.
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Params p) {
   const WsLayout L = ws_layout(p.H, p.I);
-  __shared__ int tab_expert[kMaxSlots];
-  __shared__ float tab_coef[kMaxSlots * kMaxT];
-  __shared__ int n_slots_s;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = blockIdx.x * kCombineThreads + threadIdx.x;
   const int t = e / p.H, n = e % p.H;
   const bool active = t < p.T;
@@ -845,23 +872,23 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Params p
   if (active && p.out_bias) bias = __ldg(p.out_bias + n);
   griddep_wait();
   griddep_launch();
-  if (warp == 0) {
-    const int ns = load_table(p, L, lane, tab_expert, tab_coef, false);
-    if (lane == 0) n_slots_s = ns;
-  }
-  __syncthreads();
   if (!active) return;
   const bool sh = p.sh_w13 != nullptr;
-  const int n_slots = n_slots_s;
+  // the slot count, the shared gate and every slot's partial are requested at once: one L2 round
+  // trip; slots past the count hold stale data and are masked
   const int nb = n / kDRows, r = n % kDRows;
-  float acc = 0.f;
-  for (int s = sh ? 1 : 0; s < n_slots; ++s) acc += __ldcg(partial_block(p, L, nb, s) + t * kDRows + r);
+  const float* col = partial_block(p, L, nb, 0) + t * kDRows + r;
+  const uint32_t n_slots = __ldcg(ctrl(p, L) + CTRL_NSLOTS);
+  const float gate = sh ? __ldcg(reinterpret_cast<const float*>(p.ws + L.coef) + t) : 0.f;
+  float v[kMaxSlots];
+#pragma unroll
+  for (int s = 0; s < kMaxSlots; ++s) v[s] = __ldcg(col + s * kMaxT * kDRows);
+  float acc = (!sh && n_slots > 0u) ? v[0] : 0.f;
+#pragma unroll
+  for (int s = 1; s < kMaxSlots; ++s) acc += static_cast<uint32_t>(s) < n_slots ? v[s] : 0.f;
   acc = bf16_round(acc);
   if (p.out_bias) acc = bf16_round(acc + bias);
-  if (sh) {
-    const float shv = bf16_round(__ldcg(partial_block(p, L, nb, 0) + t * kDRows + r));
-    acc += bf16_round(tab_coef[t] * shv);
-  }
+  if (sh) acc += bf16_round(gate * bf16_round(v[0]));
   p.y[static_cast<size_t>(t) * p.H + n] = __float2bfloat16_rn(acc);
 }
 
@@ -907,10 +934,21 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
   }
   static bool configured[64] = {false};
   if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(moe::expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(moe::expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-            cudaSuccess) {
+    // One shared-memory carveout for all four kernels: an SM switching carveouts between
+    // consecutive kernels must drain first, which would undo the overlap of dependent launches.
+    bool ok = cudaFuncSetAttribute(moe::expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   227 * 1024) == cudaSuccess &&
+              cudaFuncSetAttribute(moe::expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   227 * 1024) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(moe::expert_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(moe::expert_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(moe::route_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(moe::combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    if (!ok) {
       set_error("cudaFuncSetAttribute(moe) failed");
       return 2;
     }
