@@ -5,6 +5,8 @@
 #include <cstdint>
 #include <string>
 
+#include <cuda.h>
+
 namespace dm3 {
 
 constexpr int kMaxT = 4;         // activation rows handled by the skinny (decode) kernels
@@ -20,5 +22,10 @@ void set_error(const std::string& msg);
 int sm_count(int device);
 void note_launches(int n);
 bool pdl_enabled();
+// A 3-D uint8 tensor map over [d2][d1][d0] bytes (row stride stride1, plane stride stride2) whose
+// box is 128 bytes x box_rows rows x 1 plane, loaded with the 128-byte swizzle; encodings are cached
+// by their arguments. False (with the error set) when the driver rejects them.
+bool tensor_map_3d(CUtensorMap* out, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
+                   uint64_t stride2, uint32_t box_rows);
 
 }  // namespace dm3

@@ -1,0 +1,96 @@
+// Blackwell tensor-core plumbing for the drama-3 kernels (sm_100a only): TMA tensor copies into
+// 128-byte-swizzled shared memory, tcgen05 MMAs with fp32 accumulators in tensor memory (TMEM),
+// and the shared-memory / instruction descriptors they take.
+//
+// Operand layout used throughout: K-major, 128-byte swizzle. A "slab" is 128 bytes of K for a
+// block of rows; rows sit 128 bytes apart, 8-row groups 1024 bytes apart, and the 16-byte chunk c of
+// row r is stored at chunk position c ^ (r % 8). Every slab starts on a 1024-byte boundary, which
+// is what the TMA's 128B swizzle writes and what the MMA descriptor below describes.
+#pragma once
+
+#include <cuda.h>
+
+#include "dm3_common.cuh"
+
+namespace dm3 {
+namespace tc {
+
+// Byte offset of (row, k) inside a slab set of `rows_per_slab` rows (k in [0, 128 * slabs)).
+__host__ __device__ __forceinline__ uint32_t swz_offset(int row, int k, int rows_per_slab) {
+  const int slab = k >> 7, kk = k & 127;
+  return static_cast<uint32_t>(slab * rows_per_slab * 128 + (row >> 3) * 1024 + (row & 7) * 128 +
+                               ((((kk >> 4) ^ (row & 7)) << 4) | (kk & 15)));
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
+// Fields: start address >> 4 (bits 0-13), leading byte offset >> 4 = 1 (unused for this layout,
+// bits 16-29), stride byte offset 1024 >> 4 (bits 32-45), descriptor version 1 (bits 46-47),
+// layout type 2 = 128B swizzle (bits 61-63).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+  return (static_cast<uint64_t>(1) << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61) | static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+}
+
+// Instruction descriptor of kind::f8f6f4 with e4m3 A and B (both K-major), fp32 accumulate:
+// D format F32 (bits 4-5 = 1), A / B format E4M3 (0), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+__host__ __device__ constexpr uint32_t idesc_e4m3(int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- TMEM
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 8 consecutive fp32 columns of this warp's 32 TMEM lanes (one lane per thread).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------- MMA
+// D[tmem] (+)= A[smem] x B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+// Arrives once on the mbarrier when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+// 3-D tiled copy global -> shared (no multicast); completes transaction bytes on the mbarrier.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy (tensor core).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+}  // namespace tc
+}  // namespace dm3

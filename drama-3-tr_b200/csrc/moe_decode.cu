@@ -1,53 +1,63 @@
 // Decode MoE layer for B200 (sm_100a) as four chained kernels, each launched with programmatic
 // dependent launch so that a kernel's constant-weight loads start while its predecessor finishes:
 //
-//   route    router logits (exact fp64 dot products, rounded once), one warp per router row; the
-//            last CTA to finish runs softmax / top-k / renormalise and writes the slot table
-//   up       gate and up rows of every selected expert (+ the shared expert) in items of 8 + 8
-//            rows over all of H; SwiGLU in registers; h written as bf16
-//   down     64-row blocks of every selected expert's down projection against its h; routed
+//   route    router logits (exact products, summed in a hi + lo pair and rounded once), one warp
+//            per router row
+//   up       gate and up rows of every selected expert (+ the shared expert) on the tensor cores:
+//            items of 64 gate + the matching 64 up rows over all of H; SwiGLU in the epilogue;
+//            h written as bf16
+//   down     128-row blocks of every selected expert's down projection against its h; routed
 //            partials carry their routing weight
 //   combine  sum over slots per output element with the reference's rounding points (+ bias,
 //            + the sigmoid-gated shared expert), written as bf16
 //
-// Kernel boundaries are the only synchronisation between CTAs on the streaming path: a gpu-scope
-// fence issued while bulk copies are in flight costs microseconds, so none is. The one fence is in
-// the route kernel, whose CTAs have nothing in flight by then.
+// Kernel boundaries are the only synchronisation between CTAs: no gpu-scope fence or flag is
+// used on the streaming path.
 //
-// The up and down kernels run one producer warp, which stages each item with cp.async.bulk into a
-// 4-stage shared-memory ring, and two groups of four consumer warps that take alternate stages and
-// multiply the raw e4m3 weight bytes by the exact e4m3 hi / lo split of the activations (cols 0-3
-// hi of rows 0-3, cols 4-7 lo) with mma.sync m16n8k32; the per-128 block scales are applied to each
-// 128-wide k-block partial in fp32.
+// Up / down kernels (one CTA per SM, 8 warps):
+//   warp 0     TMA producer: 128-byte-swizzled weight slabs (128 rows x 128 bytes of K) into a ring
+//              of 32 KB stages, straight from the e4m3 expert tensors
+//   warp 1     MMA issuer: tcgen05.mma kind::f8f6f4, M = 128 weight rows, N = 16 activation columns
+//              (rows 0-3 the exact e4m3 "hi" split of each token, 4-7 the "lo" remainder, 8-15 zero),
+//              K = 32 per instruction; every 128-wide k block accumulates into its own 16 TMEM
+//              columns so that its block scale can be applied in fp32 afterwards
+//   warps 2-3  activation split: the tokens' bf16 rows (x, or h of the item's expert) prescaled by a
+//              power of two and split exactly into e4m3 hi + lo, written in the swizzled layout
+//   warps 4-7  epilogue: TMEM -> registers (one weight row per thread), block scales, SwiGLU or the
+//              routing weight, stores
 //
 // Ordering under programmatic dependent launch: every kernel calls griddepcontrol.launch_dependents
 // only after its own griddepcontrol.wait, so once a kernel is running, everything two launches
-// back has completed. The down kernel relies on that to read the route table before its wait.
+// back has completed. The down kernel relies on that to select experts before its wait.
 #include <cfloat>
 #include <cmath>
+#include <utility>
 
 #include "dm3_common.cuh"
 #include "dm3_internal.h"
+#include "dm3_tc.cuh"
 
 namespace dm3 {
 namespace moe {
 
-constexpr int kStages = 4;  // even: stage s belongs to consumer group s % 2
-constexpr int kGroups = 2;
-constexpr int kGroupWarps = 4;
-constexpr int kGroupThreads = kGroupWarps * 32;
-constexpr int kConsumerWarps = kGroups * kGroupWarps;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kGRows = 8;         // gate rows per up item (plus the same number of up rows)
-constexpr int kDRows = 64;        // down-projection rows per down item (= output rows per partial block)
-constexpr int kRouteWarps = 4;    // router rows per route CTA (one warp per row)
+constexpr int kThreads = 256;       // 8 warps
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpSplit = 2, kWarpEpi = 4;
+constexpr int kSplitThreads = 64;   // warps 2-3
+constexpr int kEpiThreads = 128;    // warps 4-7
+constexpr int kTileRows = 128;      // weight rows per MMA tile (M)
+constexpr int kUpHalf = 64;         // gate rows (and as many up rows) per up item
+constexpr int kBlockRows = 128;     // output rows per down item (= rows per partial block)
+constexpr int kN = 16;              // activation columns of the MMA (N)
+constexpr int kSlabBytes = kTileRows * 128;   // one 128-byte K slab of a weight tile
+constexpr int kStageBytes = 2 * kSlabBytes;   // two slabs per ring stage
+constexpr int kBSlabBytes = kN * 128;         // one K slab of the activation tile
+constexpr int kUpStages = 5, kDownStages = 6;
+constexpr int kUpAcc = 2, kDownAcc = 4;       // TMEM accumulator buffers
+constexpr uint32_t kUpTmemCols = 512, kDownTmemCols = 256;
+constexpr int kRouteWarps = 4;      // router rows per route CTA (one warp per row)
 constexpr int kCombineThreads = 256;
-constexpr int kPad = 64;          // smem row padding (bytes) of the thread-written activation tiles
-constexpr int kBarAll = 3;        // named barrier of all consumer warps (groups use 1 and 2)
-
-enum : int { ITEM_G = 2, ITEM_D = 3, ITEM_END = 5 };
+// named barriers (0 is __syncthreads)
+constexpr int kBarSelect = 1, kBarTable = 2, kBarSplit = 3;
 
 struct Params {
   int T, H, I, top_k;
@@ -79,20 +89,18 @@ struct Params {
   const float* out_bias;
   __nv_bfloat16* y;
   uint8_t* ws;
-  // scale rows travel by bulk copy when their addresses and sizes are 16-byte multiples;
-  // otherwise consumers read them from global memory
-  int sc13_bulk, sc2_bulk, sh_sc13_bulk, sh_sc2_bulk;
 };
 
+
 // ------------------------------------------------------------------ workspace layout
-// Control words, the route table, the router logits, the bf16 SwiGLU activations h and the fp32
-// per-slot partial outputs. Offsets do not depend on the row count, so one workspace serves every
-// T of a given (H, I). Only the route counter is ever non-zero between calls, and the route kernel
-// resets it.
+// Control words, the shared gate of the call, the router logits, the bf16 SwiGLU activations h and
+// the fp32 per-slot partial outputs. Offsets do not depend on the row count, so one workspace
+// serves every T of a given (H, I). Nothing in it carries state from one call to the next except
+// the sticky status word.
 struct WsLayout {
   size_t ctrl, slot_expert, coef, logits, h, h_stride, partial, total;
 };
-enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
+enum : int { CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -111,75 +119,58 @@ __host__ __device__ inline WsLayout ws_layout(int H, int I) {
   L.h_stride = align_up(static_cast<size_t>(kMaxT) * I * 2, 128);  // per slot: h[t][I] bf16
   L.h = o;
   o += L.h_stride * kMaxSlots;
-  L.partial = o;  // [H / 64][kMaxSlots][kMaxT][64] fp32: one output block's slots are adjacent
-  o += static_cast<size_t>(H / kDRows) * kMaxSlots * kMaxT * kDRows * 4;
+  L.partial = o;  // [H / 128][kMaxSlots][kMaxT][128] fp32: one output block's slots are adjacent
+  o += static_cast<size_t>(H / kBlockRows) * kMaxSlots * kMaxT * kBlockRows * 4;
   L.total = align_up(o, 256);
   return L;
 }
 
 __device__ __forceinline__ float* partial_block(const Params& p, const WsLayout& L, int nb, int slot) {
-  return reinterpret_cast<float*>(p.ws + L.partial) + (static_cast<size_t>(nb) * kMaxSlots + slot) * kMaxT * kDRows;
+  return reinterpret_cast<float*>(p.ws + L.partial) +
+         (static_cast<size_t>(nb) * kMaxSlots + slot) * kMaxT * kBlockRows;
 }
 
-// ------------------------------------------------------------------ shared-memory layout (up / down)
-struct Desc {
-  int kind, a, b, c;  // a = slot; up: b = 8-row block of gate / up rows; down: b = 64-row block
+// The route table of one call in shared memory, and the scratch that builds it.
+struct Table {
+  int expert[kMaxSlots];             // routed expert of each slot (slot 0 = shared expert when present)
+  float coef[kMaxSlots * kMaxT];     // [slot][row] routing weight (the shared slot: its sigmoid gate)
+  int sel_e[kMaxT * kMaxTopK];       // selected experts of each row, in selection order
+  float sel_w[kMaxT * kMaxTopK];     // their renormalised bf16 weights
+  float shared_coef[kMaxT];
+  int kbuf[32];
+  float wbuf[32];
 };
 
+// Barriers, the table and small per-item values of the up / down kernels.
+struct Aux {
+  uint64_t full[8], empty[8];        // TMA ring: bytes landed / MMAs done reading
+  uint64_t acc_full[4], acc_empty[4];  // TMEM accumulators: MMAs done / epilogue done reading
+  uint64_t b_ready[2], b_free[2];    // activation tiles (down): split written / epilogue done
+  uint64_t upv_full, upv_empty;      // up: up-row values written / read
+  uint32_t tmem;
+  int split_ok;
+  int n_slots;
+  float xinv[kMaxT];                 // up: 2^-e of each token's split
+  uint32_t hmax[2][kMaxT];           // down: |h| maxima of each tile's tokens (float bits)
+  float upv[kUpHalf][kMaxT];         // up: the up-row values handed to the gate-row threads
+  Table tab;
+};
+
+// Shared memory of the up / down kernels, from a 1024-byte aligned base: the ring of weight
+// stages, the activation tile(s), then Aux.
 struct SmemLayout {
-  int stage_bytes, stage, xq, grp, grp_bytes, table, misc, total;
-  int xp, hp;           // padded row pitches of the activation tiles (bytes)
-  int g_sc, d_sc, d_h;  // offsets inside a stage: up-item scales, down-item scales, staged h
+  int nstages, stage, b, b_bytes, aux, total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(int H, int I) {
+__host__ __device__ inline SmemLayout smem_layout(bool down, int H, int I) {
   SmemLayout S;
-  S.xp = H + kPad;
-  S.hp = I + kPad;
-  const int nkh = H / 128, nki = I / 128;
-  S.g_sc = 2 * kGRows * H;
-  S.d_sc = kDRows * I;
-  S.d_h = kDRows * I + kDRows * nki * 4;
-  const int g_bytes = S.g_sc + 2 * kGRows * nkh * 4;
-  const int d_bytes = S.d_h + static_cast<int>(align_up(kMaxT * I * 2, 16));
-  S.stage_bytes = static_cast<int>(align_up(g_bytes > d_bytes ? g_bytes : d_bytes, 128));
-  int o = 0;
-  S.stage = o;
-  o += kStages * S.stage_bytes;
-  S.xq = o;
-  o += 8 * S.xp;
-  // per consumer group: hq (8 x hp), red (4 warps x 32 lanes x 4 floats), h row maxima (4 floats)
-  S.grp_bytes = static_cast<int>(align_up(8 * S.hp + kGroupWarps * 32 * 16 + 16, 128));
-  S.grp = o;
-  o += kGroups * S.grp_bytes;
-  S.table = o;  // slot_expert[kMaxSlots] int, coef[kMaxSlots][kMaxT] float
-  o += static_cast<int>(align_up(kMaxSlots * 4 + kMaxSlots * kMaxT * 4 + 64, 128));
-  S.misc = o;
-  o += 512;
-  S.total = o;
+  S.nstages = down ? kDownStages : kUpStages;
+  S.stage = 0;
+  S.b = S.nstages * kStageBytes;
+  S.b_bytes = (down ? I : H) / 128 * kBSlabBytes;  // one activation tile
+  S.aux = S.b + (down ? 2 : 1) * S.b_bytes;
+  S.total = S.aux + static_cast<int>(align_up(sizeof(Aux), 128)) + 1024;  // + alignment slack
   return S;
-}
-
-struct Misc {
-  Desc desc[kStages];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  float xinv[kMaxT];
-};
-
-struct Group {  // per-consumer-group scratch
-  uint8_t* hq;
-  float* red;
-  float* hmax;
-};
-
-__device__ __forceinline__ Group group_scratch(uint8_t* smem, const SmemLayout& S, int gid) {
-  uint8_t* b = smem + S.grp + gid * S.grp_bytes;
-  Group g;
-  g.hq = b;
-  g.red = reinterpret_cast<float*>(b + 8 * S.hp);
-  g.hmax = reinterpret_cast<float*>(b + 8 * S.hp + kGroupWarps * 32 * 16);
-  return g;
 }
 
 __device__ __forceinline__ uint32_t* ctrl(const Params& p, const WsLayout& L) {
@@ -196,7 +187,7 @@ struct ExpertRef {
   const float* s13;
   const uint8_t* w2;
   const float* s2;
-  int srows, sc13_bulk, sc2_bulk;
+  int srows;
 };
 
 __device__ __forceinline__ ExpertRef expert_ref(const Params& p, int slot, const int* tab_expert) {
@@ -207,8 +198,6 @@ __device__ __forceinline__ ExpertRef expert_ref(const Params& p, int slot, const
     r.w2 = p.sh_w2;
     r.s2 = p.sh_s2;
     r.srows = p.sh_srows;
-    r.sc13_bulk = p.sh_sc13_bulk;
-    r.sc2_bulk = p.sh_sc2_bulk;
   } else {
     const int e = tab_expert[slot];
     r.w13 = p.w13 + static_cast<size_t>(e) * p.w13_stride;
@@ -216,108 +205,102 @@ __device__ __forceinline__ ExpertRef expert_ref(const Params& p, int slot, const
     r.w2 = p.w2 + static_cast<size_t>(e) * p.w2_stride;
     r.s2 = p.s2 + static_cast<size_t>(e) * p.s2_stride;
     r.srows = p.srows;
-    r.sc13_bulk = p.sc13_bulk;
-    r.sc2_bulk = p.sc2_bulk;
   }
   return r;
 }
 
 // ------------------------------------------------------------------ route table helpers
 // Builds slots from (token, expert, weight) pairs held one per lane (lanes >= n invalid).
-// Slot order: optional shared expert first, then distinct routed experts ascending.
-// Writes slot_expert / coef into the given arrays (smem or global) and returns the slot count.
-__device__ int build_slots(int lane, int n, int t, int e, float w, int shared, int T, int* slot_expert,
-                           float* coef, const float shared_coef[kMaxT]) {
+// Slot order: optional shared expert first, then distinct routed experts ascending. Returns the
+// slot count. One warp; tab.kbuf / tab.wbuf are its scratch.
+__device__ int build_slots(int lane, int n, int t, int e, float w, bool shared, int T, Table& tab) {
   const bool valid = lane < n && e >= 0;
   const int key = valid ? e : 0x7fffffff;
+  tab.kbuf[lane] = key;
+  tab.wbuf[lane] = w;
   const unsigned same = __match_any_sync(0xffffffffu, key);
   const bool first = valid && (__ffs(same) - 1 == lane);
   const unsigned firsts = __ballot_sync(0xffffffffu, first);
-  int rank = 0;
-  for (int j = 0; j < 32; ++j) {
-    const int kj = __shfl_sync(0xffffffffu, key, j);
-    if (((firsts >> j) & 1u) && kj < key) ++rank;
-  }
-  const int n_routed = __popc(firsts);
+  __syncwarp();
+  int rank = 0;  // distinct experts below this one
+  for (unsigned f = firsts; f; f &= f - 1u) rank += tab.kbuf[__ffs(f) - 1] < key ? 1 : 0;
   const int base = shared ? 1 : 0;
-  const int n_slots = base + n_routed;
   // one writer per (slot, row): a repeated pair (only possible with malformed ids) is summed in lane order
   const int key2 = valid ? ((rank << 3) | t) : -1 - lane;
   const unsigned grp = __match_any_sync(0xffffffffu, key2);
-  float wsum = 0.f;
-  for (int j = 0; j < 32; ++j) {
-    const float wj = __shfl_sync(0xffffffffu, w, j);
-    if ((grp >> j) & 1u) wsum += wj;
-  }
-  for (int i = lane; i < kMaxSlots * kMaxT; i += 32) coef[i] = 0.f;
+  for (int i = lane; i < kMaxSlots * kMaxT; i += 32) tab.coef[i] = 0.f;
   __syncwarp();
-  if (first) slot_expert[base + rank] = e;
-  if (valid && (__ffs(grp) - 1 == lane)) coef[(base + rank) * kMaxT + t] = wsum;
+  if (valid && (__ffs(grp) - 1 == lane)) {
+    float wsum = 0.f;
+    for (unsigned g = grp; g; g &= g - 1u) wsum += tab.wbuf[__ffs(g) - 1];
+    tab.expert[base + rank] = e;
+    tab.coef[(base + rank) * kMaxT + t] = wsum;
+  }
   if (shared && lane == 0) {
-    slot_expert[0] = -1;
-    for (int tt = 0; tt < T; ++tt) coef[tt] = shared_coef[tt];
+    tab.expert[0] = -1;
+    for (int tt = 0; tt < T; ++tt) tab.coef[tt] = tab.shared_coef[tt];
   }
   __syncwarp();
-  return n_slots;
+  return base + __popc(firsts);
 }
 
-// The slot table of this call, for one warp, into shared memory: built from the caller's ids /
-// weights (routing given) or copied from the table the route kernel wrote. Returns the slot count.
-__device__ int load_table(const Params& p, const WsLayout& L, int lane, int* tab_expert, float* tab_coef,
-                          bool report_bad_ids) {
-  if (p.mode == 0) {
-    const int n = p.T * p.top_k;
-    int t = 0, e = -1;
-    float w = 0.f;
-    if (lane < n) {
-      t = lane / p.top_k;
-      const int64_t id = p.ids[lane];
-      if (id >= 0 && id < p.n_experts) {
-        e = static_cast<int>(id);
-        w = __bfloat162float(p.rw[lane]);
-      } else if (report_bad_ids) {
-        flag_error(p, L, STATUS_BAD_EXPERT);
-      }
+// Route table from the caller's ids / weights (routing given), for one warp.
+__device__ int table_from_ids(const Params& p, const WsLayout& L, int lane, Table& tab, bool report_bad_ids) {
+  const int n = p.T * p.top_k;
+  int t = 0, e = -1;
+  float w = 0.f;
+  if (lane < n) {
+    t = lane / p.top_k;
+    const int64_t id = p.ids[lane];
+    if (id >= 0 && id < p.n_experts) {
+      e = static_cast<int>(id);
+      w = __bfloat162float(p.rw[lane]);
+    } else if (report_bad_ids) {
+      flag_error(p, L, STATUS_BAD_EXPERT);
     }
-    const float one[kMaxT] = {1.f, 1.f, 1.f, 1.f};
-    return build_slots(lane, n, t, e, w, p.sh_w13 != nullptr ? 1 : 0, p.T, tab_expert, tab_coef, one);
   }
-  const int n_slots = static_cast<int>(__ldcg(ctrl(p, L) + CTRL_NSLOTS));
-  const int* gse = reinterpret_cast<const int*>(p.ws + L.slot_expert);
-  const float* gco = reinterpret_cast<const float*>(p.ws + L.coef);
-  for (int i = lane; i < kMaxSlots; i += 32) tab_expert[i] = __ldcg(gse + i);
-  for (int i = lane; i < kMaxSlots * kMaxT; i += 32) tab_coef[i] = __ldcg(gco + i);
-  __syncwarp();
-  return n_slots;
+  return build_slots(lane, n, t, e, w, false, p.T, tab);
+}
+
+// Route table from the row selections route_row left in tab.sel_e / sel_w, for one warp.
+__device__ int table_from_selection(const Params& p, int lane, Table& tab) {
+  const int n = p.T * p.top_k;
+  const int t = lane < n ? lane / p.top_k : 0;
+  const int e = lane < n ? tab.sel_e[lane] : -1;
+  const float w = lane < n ? tab.sel_w[lane] : 0.f;
+  return build_slots(lane, n, t, e, w, p.sh_w13 != nullptr, p.T, tab);
 }
 
 // ------------------------------------------------------------------ route kernel
-// Router logits in shared memory of the last route CTA: [kMaxT][kMaxRouter + 1] floats (the last
-// column is the shared expert's gate), then the selected experts and weights of every row.
-struct RouteSmem {
-  float logits[kMaxT][kMaxRouter + 1];
-  int sel_e[kMaxT * kMaxTopK];
-  float sel_w[kMaxT * kMaxTopK];
-  float shared_coef[kMaxT];
-  int last;
-};
+// Order-preserving map of a float to an unsigned key (larger float, larger key; -0 and +0 equal).
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f + 0.f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
 
-// Top-k of row t by one warp from the logits in shared memory, and the renormalised weights.
-// Mirrors Speaker.__call__ (engine.py:233-235): probs = softmax(logits), (w, ids) = probs.topk(k),
-// w = (w / w.sum()).to(bf16). Selection uses the logits themselves (softmax is monotonic), ties to
-// the lower index.
-__device__ void route_row(const Params& p, RouteSmem& rs, int t, int lane) {
+// Top-k of row t by one warp from the route kernel's logits, and the renormalised weights, into
+// tab.sel_e / sel_w / shared_coef. Mirrors Speaker.__call__ (engine.py:233-235):
+// probs = softmax(logits), (w, ids) = probs.topk(k), w = (w / w.sum()).to(bf16). Selection uses the
+// logits themselves (softmax is monotonic), ties to the lower index; each step is one warp-wide
+// max of the lanes' best keys and one min of the expert indices that hold it.
+__device__ void route_row(const Params& p, const WsLayout& L, int t, int lane, Table& tab, bool write_out) {
   const int E = p.n_router, K = p.top_k;
+  const float* lg = reinterpret_cast<const float*>(p.ws + L.logits) + t * (kMaxRouter + 1);
   float lv[kMaxRouter / 32];
-  float m = -FLT_MAX;
+  uint32_t key[kMaxRouter / 32];
+#pragma unroll
+  for (int i = 0; i < kMaxRouter / 32; ++i) lv[i] = lane + 32 * i < E ? __ldcg(lg + lane + 32 * i) : -FLT_MAX;
+  const float gl = (lane == 0 && p.sh_gate) ? __ldcg(lg + E) : 0.f;
+  uint32_t kmax = 0u;
 #pragma unroll
   for (int i = 0; i < kMaxRouter / 32; ++i) {
-    const int e = lane + 32 * i;
-    lv[i] = e < E ? rs.logits[t][e] : -FLT_MAX;
-    m = fmaxf(m, lv[i]);
+    key[i] = lane + 32 * i < E ? order_key(lv[i]) : 0u;
+    kmax = max(kmax, key[i]);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float m = key_value(__reduce_max_sync(0xffffffffu, kmax));
   float z = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxRouter / 32; ++i)
@@ -325,58 +308,58 @@ __device__ void route_row(const Params& p, RouteSmem& rs, int t, int lane) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
   unsigned taken = 0u;
-  float psum = 0.f, my_p = 0.f;
   int my_e = -1;
+  float my_v = 0.f;
   for (int j = 0; j < K; ++j) {
-    float bv = -FLT_MAX;
-    int be = 0x7fffffff;
+    uint32_t bk = 0u;
+    int bi = 0;
 #pragma unroll
-    for (int i = 0; i < kMaxRouter / 32; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && !(taken & (1u << i)) && (lv[i] > bv || (lv[i] == bv && e < be))) {
-        bv = lv[i];
-        be = e;
+    for (int i = 0; i < kMaxRouter / 32; ++i)
+      if (!((taken >> i) & 1u) && key[i] > bk) {
+        bk = key[i];
+        bi = i;
       }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    if ((be & 31) == lane) taken |= 1u << (be >> 5);
-    const float pj = expf(bv - m) / z;
-    psum += pj;
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+    const uint32_t cand = (bk == mk && bk != 0u) ? static_cast<uint32_t>(lane + 32 * bi) : 0xffffffffu;
+    const uint32_t be = __reduce_min_sync(0xffffffffu, cand);
+    if (static_cast<int>(be & 31u) == lane) taken |= 1u << (be >> 5);
     if (lane == j) {
-      my_e = be;
-      my_p = pj;
+      my_e = static_cast<int>(be);
+      my_v = key_value(mk);
     }
   }
+  const float my_p = lane < K ? expf(my_v - m) / z : 0.f;
+  float psum = 0.f;
+  for (int j = 0; j < K; ++j) psum += __shfl_sync(0xffffffffu, my_p, j);
   if (lane < K) {
     const __nv_bfloat16 wb = __float2bfloat16_rn(my_p / psum);
-    rs.sel_e[t * K + lane] = my_e;
-    rs.sel_w[t * K + lane] = __bfloat162float(wb);
-    if (p.ids_out) p.ids_out[t * K + lane] = my_e;
-    if (p.w_out) p.w_out[t * K + lane] = wb;
+    tab.sel_e[t * K + lane] = my_e;
+    tab.sel_w[t * K + lane] = __bfloat162float(wb);
+    if (write_out && p.ids_out) p.ids_out[t * K + lane] = my_e;
+    if (write_out && p.w_out) p.w_out[t * K + lane] = wb;
   }
-  if (lane == 0)
-    rs.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-rs.logits[t][E]))) : 1.f;
+  if (lane == 0) tab.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-gl))) : 1.f;
 }
 
-// One warp per router row (plus the shared expert's gate row). The row is fetched into registers
-// before griddepcontrol.wait (router weights never depend on the preceding kernel); the activation
-// rows are staged in shared memory after it, all loads in flight at once. Each logit is an exact
-// fp64 dot product (bf16 x bf16 and bf16 x fp32 products are exact in fp64) rounded once to fp32
-// (then to bf16 for a bf16 router), + the optional logit bias; the shared gate row is rounded to
-// bf16 as a bf16 linear's output. The last CTA to finish (one gpu-scope fence per CTA, with no
-// copies in flight) runs the top-k of every row in parallel and writes the slot table.
+// Adds a to the unevaluated sum hi + lo without rounding error in hi (Knuth's TwoSum; the error
+// term goes to lo).
+__device__ __forceinline__ void two_sum_acc(float& hi, float& lo, float a) {
+  const float s = hi + a;
+  const float bb = s - hi;
+  lo += (hi - (s - bb)) + (a - bb);
+  hi = s;
+}
+
+// Router logits: one warp per router row (plus the shared expert's gate row). The row is fetched
+// into registers before griddepcontrol.wait (router weights never depend on the preceding kernel);
+// the activation rows are staged in shared memory after it, all loads in flight at once. Every
+// product is exact in fp32 (bf16 x bf16; bf16 x fp32 keeps its rounding error through an fma) and
+// is summed as a hi + lo pair, which carries about 48 significant bits, so the logit is the sum
+// rounded once to fp32 (then to bf16 for a bf16 router), + the optional logit bias. The shared gate
+// row is rounded to bf16 as a bf16 linear's output. The top-k runs in the kernels that use it.
 __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p) {
   const WsLayout L = ws_layout(p.H, p.I);
   __shared__ __align__(16) __nv_bfloat16 xs[kMaxT * kMaxH];
-  __shared__ RouteSmem rs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool sh_gate_row = p.sh_w13 != nullptr && p.sh_gate != nullptr;
   const int rows = p.n_router + (sh_gate_row ? 1 : 0);
@@ -415,88 +398,92 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p)
     }
   }
   __syncthreads();
+  if (row >= rows) return;
   float* logits = reinterpret_cast<float*>(p.ws + L.logits);
-  if (row < rows) {
-    for (int t = 0; t < p.T; ++t) {
-      const __nv_bfloat16* xr = xs + t * p.H;
-      double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int t = 0; t < p.T; ++t) {
+    const __nv_bfloat16* xr = xs + t * p.H;
+    float hi[4] = {0.f, 0.f, 0.f, 0.f}, lo[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < kMaxChunks; ++j) {
-        if (j < chunks) {
-          if (row_f32) {
-            const float* w = reinterpret_cast<const float*>(&wv[j]);
-            const uint2 xv = *reinterpret_cast<const uint2*>(xr + lane * 4 + 128 * j);
-            const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+    for (int j = 0; j < kMaxChunks; ++j) {
+      if (j < chunks) {
+        if (row_f32) {
+          const float* w = reinterpret_cast<const float*>(&wv[j]);
+          const uint2 xv = *reinterpret_cast<const uint2*>(xr + lane * 4 + 128 * j);
+          const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              acc[i] = fma(static_cast<double>(__bfloat162float(xe[i])), static_cast<double>(w[i]), acc[i]);
-          } else {
-            const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
-            const uint4 xv = *reinterpret_cast<const uint4*>(xr + lane * 8 + 256 * j);
-            const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              acc[i & 3] = fma(static_cast<double>(__bfloat162float(xe[i])),
-                               static_cast<double>(__bfloat162float(w[i])), acc[i & 3]);
+          for (int i = 0; i < 4; ++i) {
+            const float xf = __bfloat162float(xe[i]);
+            const float pr = xf * w[i];
+            lo[i] += fmaf(xf, w[i], -pr);  // the product's rounding error, exact
+            two_sum_acc(hi[i], lo[i], pr);
           }
-        }
-      }
-      double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) {
-        float v = __double2float_rn(sum);
-        if (is_router) {
-          if (p.logits_bf16) v = bf16_round(v);
-          if (p.logit_bias) v += p.logit_bias[row];
         } else {
-          v = bf16_round(v);
+          const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
+          const uint4 xv = *reinterpret_cast<const uint4*>(xr + lane * 8 + 256 * j);
+          const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            two_sum_acc(hi[i & 3], lo[i & 3], __bfloat162float(xe[i]) * __bfloat162float(w[i]));
         }
-        logits[t * (kMaxRouter + 1) + row] = v;
       }
     }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t old = atomicAdd(ctrl(p, L) + CTRL_ROUTE_COUNT, 1u);
-    rs.last = old == gridDim.x - 1;
-    if (rs.last) __threadfence();
-  }
-  __syncthreads();
-  if (!rs.last) return;
-  // last CTA: every logit is visible; stage them, one warp per row for the top-k, then the table
-  for (int i = threadIdx.x; i < p.T * (kMaxRouter + 1); i += kRouteWarps * 32) {
-    const int t = i / (kMaxRouter + 1), e = i % (kMaxRouter + 1);
-    rs.logits[t][e] = e < rows ? __ldcg(logits + i) : 0.f;
-  }
-  __syncthreads();
-  if (warp < p.T) route_row(p, rs, warp, lane);
-  __syncthreads();
-  if (warp == 0) {
-    const int K = p.top_k;
-    const int n = p.T * K;
-    const int my_t = lane < n ? lane / K : 0;
-    const int my_e = lane < n ? rs.sel_e[lane] : -1;
-    const float my_w = lane < n ? rs.sel_w[lane] : 0.f;
-    int* slot_expert = reinterpret_cast<int*>(p.ws + L.slot_expert);
-    float* coef = reinterpret_cast<float*>(p.ws + L.coef);
-    const int n_slots = build_slots(lane, n, my_t, my_e, my_w, p.sh_w13 != nullptr, p.T, slot_expert, coef,
-                                    rs.shared_coef);
+    float h = hi[0], l = lo[0];
+#pragma unroll
+    for (int i = 1; i < 4; ++i) {
+      l += lo[i];
+      two_sum_acc(h, l, hi[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float oh = __shfl_xor_sync(0xffffffffu, h, o);
+      l += __shfl_xor_sync(0xffffffffu, l, o);
+      two_sum_acc(h, l, oh);
+    }
     if (lane == 0) {
-      ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(n_slots);
-      ctrl(p, L)[CTRL_ROUTE_COUNT] = 0u;  // every CTA has counted: ready for the next call
+      float v = h + l;
+      if (is_router) {
+        if (p.logits_bf16) v = bf16_round(v);
+        if (p.logit_bias) v += p.logit_bias[row];
+      } else {
+        v = bf16_round(v);
+      }
+      logits[t * (kMaxRouter + 1) + row] = v;
     }
   }
 }
 
-// ------------------------------------------------------------------ up: x split
-// Each of the first T consumer warps loads one activation row and writes its exact e4m3 hi / lo
-// split (prescaled by a power of two) as B-operand columns.
-__device__ void prepare_x(const Params& p, uint8_t* xq, Misc* misc, int warp, int lane, int xp) {
-  const int H = p.H;
-  if (warp < p.T) {
-    const __nv_bfloat16* xr = p.x + static_cast<size_t>(warp) * H;
+// ------------------------------------------------------------------ activation split
+// 16 consecutive bf16 values, prescaled by sc, split exactly into e4m3 hi and lo bytes.
+__device__ __forceinline__ void split16(const uint4 (&v)[2], float sc, uint4& hi, uint4& lo) {
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(v);
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint16_t h0, l0, h1, l1;
+    split2(__bfloat162float(e[4 * i]) * sc, __bfloat162float(e[4 * i + 1]) * sc, h0, l0);
+    split2(__bfloat162float(e[4 * i + 2]) * sc, __bfloat162float(e[4 * i + 3]) * sc, h1, l1);
+    h[i] = h0 | (static_cast<uint32_t>(h1) << 16);
+    l[i] = l0 | (static_cast<uint32_t>(l1) << 16);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ float abs_max16(const uint4 (&v)[2]) {
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(v);
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(__bfloat162float(e[i])));
+  return m;
+}
+
+// Up: the activation tile of all H. Row t holds the e4m3 hi part of x[t] * 2^e_t (e_t maps the
+// row's absolute maximum into [128, 256)), row 4 + t the lo remainder, every other row zero.
+// Run by the 64 split threads; they fence their writes for the tensor core.
+__device__ void split_x(const Params& p, uint8_t* bt, Aux& aux, int ptid) {
+  const int H = p.H, wl = ptid >> 5, lane = ptid & 31;
+  for (int t = wl; t < p.T; t += 2) {
+    const __nv_bfloat16* xr = p.x + static_cast<size_t>(t) * H;
     float amax = 0.f;
     for (int k = lane * 8; k < H; k += 256) {
       const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
@@ -506,357 +493,439 @@ __device__ void prepare_x(const Params& p, uint8_t* xq, Misc* misc, int warp, in
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const int e = split_exponent(amax);
-    const float sc = exp2i(e);
-    if (lane == 0) misc->xinv[warp] = exp2i(-e);
-    uint8_t* hi = xq + warp * xp;
-    uint8_t* lo = xq + (4 + warp) * xp;
-    for (int k = lane * 8; k < H; k += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-      const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&v);
-      uint16_t h4[4], l4[4];
+    if (lane == 0) {
+      aux.hmax[0][t] = __float_as_uint(amax);
+      aux.xinv[t] = exp2i(-split_exponent(amax));
+    }
+  }
+  named_bar(kBarSplit, kSplitThreads);
+  const int chunks = H / 16;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int task = ptid; task < kMaxT * chunks; task += kSplitThreads) {
+    const int t = task / chunks, c = task % chunks;
+    uint4 hi = z, lo = z;
+    if (t < p.T) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * H + c * 16);
+      const uint4 v[2] = {src[0], src[1]};
+      split16(v, exp2i(split_exponent(__uint_as_float(aux.hmax[0][t]))), hi, lo);
+    }
+    *reinterpret_cast<uint4*>(bt + tc::swz_offset(t, c * 16, kN)) = hi;
+    *reinterpret_cast<uint4*>(bt + tc::swz_offset(4 + t, c * 16, kN)) = lo;
+  }
+  for (int i = ptid; i < (H / 128) * 64; i += kSplitThreads)  // rows 8-15 of every slab
+    *reinterpret_cast<uint4*>(bt + (i / 64) * kBSlabBytes + 1024 + (i % 64) * 16) = z;
+  tc::fence_proxy_async_smem();
+}
+
+// Down: the activation tile of one slot's h (rows t < T; the zero rows are written once per
+// kernel). hmax receives each row's absolute maximum for the epilogue.
+__device__ void split_h(const Params& p, const WsLayout& L, uint8_t* bt, uint32_t* hmax, int slot, int ptid) {
+  const int I = p.I, chunks = I / 16, n = p.T * chunks;
+  constexpr int kMaxTasks = kMaxT * kMaxI / 16 / kSplitThreads;
+  if (ptid < kMaxT) hmax[ptid] = 0u;
+  named_bar(kBarSplit, kSplitThreads);
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(p.ws + L.h + static_cast<size_t>(slot) * L.h_stride);
+  uint4 v[kMaxTasks][2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        split2(__bfloat162float(e8[2 * i]) * sc, __bfloat162float(e8[2 * i + 1]) * sc, h4[i], l4[i]);
-      *reinterpret_cast<uint2*>(hi + k) = make_uint2(h4[0] | (uint32_t(h4[1]) << 16), h4[2] | (uint32_t(h4[3]) << 16));
-      *reinterpret_cast<uint2*>(lo + k) = make_uint2(l4[0] | (uint32_t(l4[1]) << 16), l4[2] | (uint32_t(l4[3]) << 16));
+  for (int q = 0; q < kMaxTasks; ++q) {
+    const int task = ptid + q * kSplitThreads;
+    if (task < n) {
+      const uint4* src = reinterpret_cast<const uint4*>(h + (task / chunks) * I + (task % chunks) * 16);
+      v[q][0] = __ldcg(src);
+      v[q][1] = __ldcg(src + 1);
+      atomicMax(&hmax[task / chunks], __float_as_uint(abs_max16(v[q])));
+    }
+  }
+  named_bar(kBarSplit, kSplitThreads);
+#pragma unroll
+  for (int q = 0; q < kMaxTasks; ++q) {
+    const int task = ptid + q * kSplitThreads;
+    if (task < n) {
+      const int t = task / chunks, c = task % chunks;
+      uint4 hi, lo;
+      split16(v[q], exp2i(split_exponent(__uint_as_float(hmax[t]))), hi, lo);
+      *reinterpret_cast<uint4*>(bt + tc::swz_offset(t, c * 16, kN)) = hi;
+      *reinterpret_cast<uint4*>(bt + tc::swz_offset(4 + t, c * 16, kN)) = lo;
+    }
+  }
+  tc::fence_proxy_async_smem();
+}
+
+// ------------------------------------------------------------------ epilogues
+// Sum over k blocks of scale x (hi + lo) for this thread's weight row, from nkb accumulators of
+// 16 TMEM columns each starting at column `col`.
+template <int MaxKb>
+__device__ __forceinline__ void reduce_kblocks(uint32_t taddr, int nkb, const float* sc, float (&acc)[kMaxT]) {
+#pragma unroll
+  for (int t = 0; t < kMaxT; ++t) acc[t] = 0.f;
+#pragma unroll
+  for (int kb0 = 0; kb0 < MaxKb; kb0 += 8) {
+    if (kb0 < nkb) {
+      float v[8][8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (kb0 + j < nkb) tc::tmem_ld8(taddr + (kb0 + j) * 16, v[j]);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (kb0 + j < nkb)
+#pragma unroll
+          for (int t = 0; t < kMaxT; ++t) acc[t] = fmaf(sc[kb0 + j], v[j][t] + v[j][4 + t], acc[t]);
     }
   }
 }
 
-// ------------------------------------------------------------------ up: one item
-// 8 gate rows (tile rows 0-7) and the matching 8 up rows (tile rows 8-15) of one expert against the
-// split activations: lane (g, q) ends with gate row g and up row g for rows 2q, 2q+1 (hi columns,
-// after folding the lo columns in), so SwiGLU happens in registers. The group's 4 warps split the
-// 128-wide k blocks and reduce through shared memory.
-__device__ void consume_g(const Params& p, const WsLayout& L, const SmemLayout& S, const uint8_t* xq,
-                          const uint8_t* stage, const Desc& d, const Misc* misc, const Group& G, const int* tab_expert,
-                          int gw, int lane, int bar_id) {
-  const int H = p.H;
-  const int g = lane >> 2, q = lane & 3;
-  const int nkb = H / 128;
-  const int slot = d.a;
-  const ExpertRef ex = expert_ref(p, slot, tab_expert);
-  const float* sc = reinterpret_cast<const float*>(stage + S.g_sc);
-  const int gate_row = d.b * kGRows + g, up_row = p.I + d.b * kGRows + g;
-  const int sg_row = ex.srows == 1 ? g : 0;  // index into the staged gate scale rows
-  const uint8_t* row_lo = stage + g * H;
-  const uint8_t* row_hi = stage + (kGRows + g) * H;
-  const uint8_t* bcol = xq + g * S.xp;
-  const bool bvalid = (g & 3) < p.T;
-  float tot[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int kb0 = gw; kb0 < nkb; kb0 += 2 * kGroupWarps) {
-    const int kb1 = kb0 + kGroupWarps;
-    const bool v1 = kb1 < nkb;
-    const int kbs[2] = {kb0, v1 ? kb1 : kb0};
-    float part[2][4];
-    tile_kblocks<2>(part, row_lo, row_hi, bcol, true, true, bvalid, kbs, q);
+// Up: thread r holds gate row 64*blk + r (r < 64) or up row I + 64*blk + r - 64; the up values go
+// through shared memory to the gate threads, which apply SwiGLU and store h. Releases the
+// accumulator buffer (acc_empty) as soon as it has been read.
+__device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32_t taddr, uint64_t* acc_empty,
+                            int slot, int blk, int e, int lane, int k) {
+  const int r = 32 * e + lane;
+  const int nkb = p.H / 128;
+  const ExpertRef ex = expert_ref(p, slot, aux.tab.expert);
+  const int wrow = r < kUpHalf ? kUpHalf * blk + r : p.I + kUpHalf * blk + (r - kUpHalf);
+  const float* srow = ex.s13 + static_cast<size_t>(wrow / ex.srows) * nkb;
+  float sc[kMaxH / 128];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      if (i == 1 && !v1) break;
-      float sgv, suv;
-      if (ex.sc13_bulk) {
-        sgv = sc[sg_row * nkb + kbs[i]];
-        suv = sc[(kGRows + sg_row) * nkb + kbs[i]];
-      } else {
-        sgv = __ldg(ex.s13 + static_cast<size_t>(gate_row / ex.srows) * nkb + kbs[i]);
-        suv = __ldg(ex.s13 + static_cast<size_t>(up_row / ex.srows) * nkb + kbs[i]);
-      }
-      tot[0] = fmaf(part[i][0], sgv, tot[0]);
-      tot[1] = fmaf(part[i][1], sgv, tot[1]);
-      tot[2] = fmaf(part[i][2], suv, tot[2]);
-      tot[3] = fmaf(part[i][3], suv, tot[3]);
-    }
+  for (int kb = 0; kb < kMaxH / 128; ++kb) sc[kb] = kb < nkb ? __ldg(srow + kb) : 0.f;
+  float acc[kMaxT];
+  reduce_kblocks<kMaxH / 128>(taddr, nkb, sc, acc);
+  tc::fence_before_sync();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(acc_empty);
+  // hand-off of the up values through shared memory, guarded by two mbarriers (bounded waits)
+  const uint32_t par = static_cast<uint32_t>(k & 1);
+  if (r >= kUpHalf) {
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait(&aux.upv_empty, par ^ 1u);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok && lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t) aux.upv[r - kUpHalf][t] = acc[t] * aux.xinv[t];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&aux.upv_full);
+    return;
   }
-  // fold lo columns (q = 2, 3) onto hi columns (q = 0, 1)
-#pragma unroll
-  for (int i = 0; i < 4; ++i) tot[i] += __shfl_down_sync(0xffffffffu, tot[i], 2);
-  *reinterpret_cast<float4*>(G.red + (gw * 32 + lane) * 4) = make_float4(tot[0], tot[1], tot[2], tot[3]);
-  named_bar(bar_id, kGroupThreads);
-  if (gw == 0 && q < 2) {
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int w = 0; w < kGroupWarps; ++w) {
-      const float4 r = *reinterpret_cast<const float4*>(G.red + (w * 32 + lane) * 4);
-      v[0] += r.x;
-      v[1] += r.y;
-      v[2] += r.z;
-      v[3] += r.w;
-    }
+  bool ok = true;
+  if (lane == 0) ok = mbar_wait(&aux.upv_full, par);
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) {
+    if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+    return;
+  }
+  {
     const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
     __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.ws + L.h + static_cast<size_t>(slot) * L.h_stride);
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int t = 2 * q + c;
-      if (t < p.T) {
-        float gt = v[c] * misc->xinv[t];
-        float ut = v[2 + c] * misc->xinv[t];
-        float hv;
-        if (shared_slot) {
-          // the shared expert is a chain of bf16 modules: down(silu(gate(x)) * up(x))
-          gt = bf16_round(gt);
-          ut = bf16_round(ut);
-          hv = bf16_round(gt / (1.f + expf(-gt))) * ut;
-        } else {
-          hv = gt / (1.f + expf(-gt)) * ut;
-        }
-        h[static_cast<size_t>(t) * p.I + gate_row] = __float2bfloat16_rn(hv);
+    for (int t = 0; t < p.T; ++t) {
+      float gt = acc[t] * aux.xinv[t];
+      float ut = aux.upv[r][t];
+      float hv;
+      if (shared_slot) {
+        // the shared expert is a chain of bf16 modules: down(silu(gate(x)) * up(x))
+        gt = bf16_round(gt);
+        ut = bf16_round(ut);
+        hv = bf16_round(gt / (1.f + expf(-gt))) * ut;
+      } else {
+        hv = gt / (1.f + expf(-gt)) * ut;
       }
+      h[static_cast<size_t>(t) * p.I + kUpHalf * blk + r] = __float2bfloat16_rn(hv);
     }
   }
-  named_bar(bar_id, kGroupThreads);  // red is reused by the group's next item
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&aux.upv_empty);  // upv may be rewritten for the next item
 }
 
-// ------------------------------------------------------------------ down: one item
-// 64 rows of one expert's down projection against its staged h: the group finds each row's
-// absolute maximum, writes the exact e4m3 hi / lo split, then each warp owns 16 rows over all of I.
-// Routed slots carry their routing weight into the partial; the shared slot stays raw (the combine
-// kernel rounds and gates it).
-__device__ void consume_d(const Params& p, const WsLayout& L, const SmemLayout& S, const uint8_t* stage,
-                          const Desc& d, const Group& G, const float* coef_tab, const int* tab_expert, int gw,
-                          int lane, int gtid, int bar_id) {
-  const int I = p.I, T = p.T;
-  const int nkb = I / 128;
-  const int slot = d.a;
-  const ExpertRef ex = expert_ref(p, slot, tab_expert);
-  const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(stage + S.d_h);
-  const float* sc = reinterpret_cast<const float*>(stage + S.d_sc);
-  if (gw < T) {  // warp t: the absolute maximum of h row t
-    float am = 0.f;
-    for (int k = lane * 8; k < I; k += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(hv + static_cast<size_t>(gw) * I + k);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+// Down: thread r holds output row 128*nb + r of one slot; the partial is weighted by the routing
+// weight (the shared slot stays raw: the combine kernel rounds and gates it). Releases the
+// accumulator buffer and the activation tile once both have been read.
+__device__ void epilogue_down(const Params& p, const WsLayout& L, Aux& aux, uint32_t taddr, uint64_t* acc_empty,
+                              uint64_t* b_free, const uint32_t* hmax, int slot, int nb, int e, int lane) {
+  const int r = 32 * e + lane, n = kBlockRows * nb + r;
+  const int nkb = p.I / 128;
+  const ExpertRef ex = expert_ref(p, slot, aux.tab.expert);
+  const float* srow = ex.s2 + static_cast<size_t>(n / ex.srows) * nkb;
+  float sc[kMaxI / 128];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(__bfloat162float(e[i])));
-    }
+  for (int kb = 0; kb < kMaxI / 128; ++kb) sc[kb] = kb < nkb ? __ldg(srow + kb) : 0.f;
+  float acc[kMaxT];
+  reduce_kblocks<kMaxI / 128>(taddr, nkb, sc, acc);
+  tc::fence_before_sync();
+  float k[kMaxT];
+  const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    if (lane == 0) G.hmax[gw] = am;
+  for (int t = 0; t < kMaxT; ++t)
+    k[t] = exp2i(-split_exponent(__uint_as_float(hmax[t]))) * (shared_slot ? 1.f : aux.tab.coef[slot * kMaxT + t]);
+  __syncwarp();
+  if (lane == 0) {
+    mbar_arrive(acc_empty);
+    mbar_arrive(b_free);
   }
-  named_bar(bar_id, kGroupThreads);
-  for (int i = gtid; i < T * I / 2; i += kGroupThreads) {
-    const int t = (2 * i) / I, k = (2 * i) % I;
-    const float s = exp2i(split_exponent(G.hmax[t]));
-    uint16_t hi, lo;
-    split2(__bfloat162float(hv[2 * i]) * s, __bfloat162float(hv[2 * i + 1]) * s, hi, lo);
-    *reinterpret_cast<uint16_t*>(G.hq + t * S.hp + k) = hi;
-    *reinterpret_cast<uint16_t*>(G.hq + (4 + t) * S.hp + k) = lo;
-  }
-  named_bar(bar_id, kGroupThreads);
-  const int g = lane >> 2, q = lane & 3;
-  const int r_lo = gw * 16 + g, r_hi = gw * 16 + 8 + g;
-  const uint8_t* row_lo = stage + r_lo * I;
-  const uint8_t* row_hi = stage + r_hi * I;
-  const uint8_t* bcol = G.hq + g * S.hp;
-  const bool bvalid = (g & 3) < T;
-  const int n_lo = d.b * kDRows + r_lo, n_hi = d.b * kDRows + r_hi;
-  float tot[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int kb0 = 0; kb0 < nkb; kb0 += 2) {
-    const bool v1 = kb0 + 1 < nkb;
-    const int kbs[2] = {kb0, v1 ? kb0 + 1 : kb0};
-    float part[2][4];
-    tile_kblocks<2>(part, row_lo, row_hi, bcol, true, true, bvalid, kbs, q);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      if (i == 1 && !v1) break;
-      float s0, s1;
-      if (ex.sc2_bulk) {
-        s0 = sc[(ex.srows == 1 ? r_lo : 0) * nkb + kbs[i]];
-        s1 = sc[(ex.srows == 1 ? r_hi : 0) * nkb + kbs[i]];
-      } else {
-        s0 = __ldg(ex.s2 + static_cast<size_t>(n_lo / ex.srows) * nkb + kbs[i]);
-        s1 = __ldg(ex.s2 + static_cast<size_t>(n_hi / ex.srows) * nkb + kbs[i]);
-      }
-      tot[0] = fmaf(part[i][0], s0, tot[0]);
-      tot[1] = fmaf(part[i][1], s0, tot[1]);
-      tot[2] = fmaf(part[i][2], s1, tot[2]);
-      tot[3] = fmaf(part[i][3], s1, tot[3]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) tot[i] += __shfl_down_sync(0xffffffffu, tot[i], 2);
-  if (q < 2) {
-    float* part = partial_block(p, L, d.b, slot);
-    const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int t = 2 * q + c;
-      if (t < T) {
-        const float k = exp2i(-split_exponent(G.hmax[t])) * (shared_slot ? 1.f : coef_tab[slot * kMaxT + t]);
-        __stcg(part + t * kDRows + r_lo, tot[c] * k);
-        __stcg(part + t * kDRows + r_hi, tot[2 + c] * k);
-      }
-    }
-  }
-  named_bar(bar_id, kGroupThreads);  // hq / hmax are reused by the group's next item
+  float* part = partial_block(p, L, nb, slot);
+  for (int t = 0; t < p.T; ++t) __stcg(part + t * kBlockRows + r, acc[t] * k[t]);
 }
 
 // ------------------------------------------------------------------ up / down kernels
 // One body for both streaming kernels (DOWN = false: up items, true: down items). Items are
 // assigned statically (CTA c takes items c, c + gridDim, ...), so CTAs never wait on each other.
+// map_w covers the routed experts ([E][rows][K] bytes), map_sh the shared expert.
+//
+// Route table: with the router in the layer, epilogue warps 4 .. 4+T-1 select one row's experts
+// each (up: after the wait, since the route kernel is the predecessor; down: before it, since the
+// route kernel has completed by the time the down kernel starts) and warp 4 builds the table; with
+// routing given, warp 4 builds it from the caller's ids.
 template <bool DOWN>
-__global__ void __launch_bounds__(kThreads, 1) expert_kernel(const Params p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const SmemLayout S = smem_layout(p.H, p.I);
+__global__ void __launch_bounds__(kThreads, 1)
+    expert_kernel(const Params p, const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_sh) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const SmemLayout S = smem_layout(DOWN, p.H, p.I);
   const WsLayout L = ws_layout(p.H, p.I);
-  Misc* misc = reinterpret_cast<Misc*>(smem + S.misc);
-  int* tab_expert = reinterpret_cast<int*>(smem + S.table);
-  float* tab_coef = reinterpret_cast<float*>(smem + S.table + kMaxSlots * 4);
+  Aux& aux = *reinterpret_cast<Aux*>(smem + S.aux);
+  Table& tab = aux.tab;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool sh = p.sh_w13 != nullptr;
-  const int per_slot = DOWN ? p.H / kDRows : p.I / kGRows;
+  const int per_slot = DOWN ? p.H / kBlockRows : p.I / kUpHalf;
+  const int nkb = (DOWN ? p.I : p.H) / 128;  // 128-wide k blocks (slabs) per item
+  const int nchunks = (nkb + 1) / 2;         // ring stages per item
+  const int nacc = DOWN ? kDownAcc : kUpAcc;
+  const uint32_t acc_cols = DOWN ? kDownTmemCols / kDownAcc : kUpTmemCols / kUpAcc;
+  const uint32_t tmem_cols = DOWN ? kDownTmemCols : kUpTmemCols;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&misc->full[s], 1);             // the producer's arrive.expect_tx; the bytes complete it
-      mbar_init(&misc->empty[s], kGroupWarps);  // the owning group's warps
+    for (int s = 0; s < S.nstages; ++s) {
+      mbar_init(&aux.full[s], 1);   // the producer's arrive.expect_tx; the TMA bytes complete it
+      mbar_init(&aux.empty[s], 1);  // tcgen05.commit after the stage's MMAs
     }
+    for (int a = 0; a < nacc; ++a) {
+      mbar_init(&aux.acc_full[a], 1);           // tcgen05.commit after the item's last MMA
+      mbar_init(&aux.acc_empty[a], kEpiThreads / 32);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&aux.b_ready[b], kSplitThreads);
+      mbar_init(&aux.b_free[b], kEpiThreads / 32);
+    }
+    mbar_init(&aux.upv_full, 2);   // the two up-row warps
+    mbar_init(&aux.upv_empty, 2);  // the two gate-row warps
     fence_mbar_init();
   }
+  if (warp == kWarpMma) tc::tmem_alloc(&aux.tmem, tmem_cols);
+  if (DOWN && warp >= kWarpSplit && warp < kWarpEpi) {
+    // the rows of the activation tiles that no item writes stay zero
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid - kWarpSplit * 32; i < 2 * S.b_bytes / 16; i += kSplitThreads)
+      reinterpret_cast<uint4*>(smem + S.b)[i] = z;
+    tc::fence_proxy_async_smem();
+  }
+  tc::fence_before_sync();
   __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = aux.tmem;
 
-  if (warp == kProducerWarp) {
-    // ================================================================ producer
-    // Up: shared-expert items need no routing and are staged before griddepcontrol.wait; the table
-    // (the route kernel's, or built from ids a preceding kernel wrote) is read after it.
-    // Down: the route table is final before this kernel starts, so weights are staged before the
-    // wait; h comes from the up kernel and is staged after it.
-    bool waited = false;
-    int n_slots = sh ? 1 : 0;
-    bool have_table = false;
-    int pend[kStages];  // stages whose h copy waits for the up kernel (down, before the wait)
-    int npend = 0;
-    auto get_table = [&]() {
-      n_slots = load_table(p, L, lane, tab_expert, tab_coef, !DOWN);
-      have_table = true;
-      // with routing given, the up kernel publishes the slot count for the combine kernel (after its
-      // wait, so the previous call's combine has finished reading it)
-      if (!DOWN && p.mode == 0 && blockIdx.x == 0 && lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(n_slots);
-    };
-    auto wait_predecessor = [&]() {
-      griddep_wait();
-      griddep_launch();
-      waited = true;
-      if (DOWN) {
-        if (lane == 0) {
-          fence_proxy_async();
-          for (int i = 0; i < npend; ++i)
-            bulk_g2s(smem + S.stage + pend[i] * S.stage_bytes + S.d_h,
-                     p.ws + L.h + static_cast<size_t>(misc->desc[pend[i]].a) * L.h_stride,
-                     static_cast<uint32_t>(p.T) * p.I * 2, &misc->full[pend[i]]);
-        }
-        npend = 0;
-        __syncwarp();
-      }
-    };
-    if (DOWN) get_table();
+  if (warp == kWarpTma) {
+    // ================================================================ TMA producer
     int stage = 0;
     uint32_t empty_par = 1;
-    for (int idx = blockIdx.x;; idx += gridDim.x) {
-      if (!DOWN && !have_table && !(sh && idx < per_slot)) {
-        wait_predecessor();
-        get_table();
+    bool ok = true;
+    auto issue = [&](int idx, int c) -> bool {
+      bool ready = true;
+      if (lane == 0) ready = mbar_wait(&aux.empty[stage], empty_par);
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) {
+        if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+        return false;
       }
-      if (idx >= n_slots * per_slot) break;
-      if (DOWN && !waited && npend == kStages) wait_predecessor();  // every stage waits for its h
-      const Desc d{DOWN ? ITEM_D : ITEM_G, idx / per_slot, idx % per_slot, 0};
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&misc->empty[stage], empty_par);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
+      if (lane == 0) {
+        const int slot = idx / per_slot, blk = idx % per_slot;
+        const bool shared_slot = sh && slot == 0;
+        const CUtensorMap* map = shared_slot ? &map_sh : &map_w;
+        const int ex = shared_slot ? 0 : tab.expert[slot];
+        uint8_t* dst = smem + S.stage + stage * kStageBytes;
+        const int kb0 = 2 * c, nsl = min(2, nkb - kb0);
+        mbar_arrive_expect_tx(&aux.full[stage], static_cast<uint32_t>(nsl * kSlabBytes));
+        for (int j = 0; j < nsl; ++j) {
+          const int kx = (kb0 + j) * 128;
+          if (!DOWN) {
+            tc::tma_load_3d(dst + j * kSlabBytes, map, kx, kUpHalf * blk, ex, &aux.full[stage]);
+            tc::tma_load_3d(dst + j * kSlabBytes + kSlabBytes / 2, map, kx, p.I + kUpHalf * blk, ex, &aux.full[stage]);
+          } else {
+            tc::tma_load_3d(dst + j * kSlabBytes, map, kx, kBlockRows * blk, ex, &aux.full[stage]);
+          }
+        }
+      }
+      __syncwarp();
+      if (++stage == S.nstages) {
+        stage = 0;
+        empty_par ^= 1u;
+      }
+      return true;
+    };
+    if (lane == 0) {
+      tc::prefetch_map(&map_w);
+      if (sh) tc::prefetch_map(&map_sh);
+    }
+    int k = 0, c = 0;  // item ordinal and chunk of the next stage
+    if (!DOWN && sh) {
+      // shared-expert stages need no routing: up to one ring of them before the table exists
+      for (int n = 0; ok && n < S.nstages; ++n) {
+        const int idx = blockIdx.x + k * gridDim.x;
+        if (idx >= per_slot) break;
+        ok = issue(idx, c);
+        if (++c == nchunks) {
+          c = 0;
+          ++k;
+        }
+      }
+    }
+    named_bar(kBarSelect, kThreads);
+    named_bar(kBarTable, kThreads);
+    const int n_items = aux.n_slots * per_slot;
+    while (ok) {
+      const int idx = blockIdx.x + k * gridDim.x;
+      if (idx >= n_items) break;
+      ok = issue(idx, c);
+      if (++c == nchunks) {
+        c = 0;
+        ++k;
+      }
+    }
+  } else if (warp == kWarpMma) {
+    // ================================================================ MMA issuer
+    named_bar(kBarSelect, kThreads);
+    named_bar(kBarTable, kThreads);
+    tc::fence_after_sync();
+    const int n_items = aux.n_slots * per_slot;
+    const uint32_t idesc = tc::idesc_e4m3(kTileRows, kN);
+    int stage = 0;
+    uint32_t full_par = 0;
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+      const int idx = blockIdx.x + k * gridDim.x;
+      if (idx >= n_items) break;
+      const int ab = k % nacc, bb = k & 1;
+      bool ready = true;
+      if (lane == 0) {
+        ready = mbar_wait(&aux.acc_empty[ab], ((k / nacc) & 1) ^ 1u);
+        if (ready && DOWN) ready = mbar_wait(&aux.b_ready[bb], (k >> 1) & 1);
+      }
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) {
         if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
         break;
       }
-      uint8_t* st = smem + S.stage + stage * S.stage_bytes;
-      uint64_t* full = &misc->full[stage];
-      if (lane == 0) {
-        misc->desc[stage] = d;
-        const ExpertRef ex = expert_ref(p, d.a, tab_expert);
-        if (!DOWN) {
-          const int nkb = p.H / 128;
-          const int r0 = d.b * kGRows, u0 = p.I + d.b * kGRows;
-          const uint32_t blk = kGRows * p.H;
-          const uint32_t n = ex.srows == 1 ? kGRows * nkb * 4 : nkb * 4;
-          mbar_arrive_expect_tx(full, 2 * blk + (ex.sc13_bulk ? 2 * n : 0u));
-          bulk_g2s(st, ex.w13 + static_cast<size_t>(r0) * p.H, blk, full);
-          bulk_g2s(st + blk, ex.w13 + static_cast<size_t>(u0) * p.H, blk, full);
-          if (ex.sc13_bulk) {
-            float* sd = reinterpret_cast<float*>(st + S.g_sc);
-            bulk_g2s(sd, ex.s13 + static_cast<size_t>(r0 / ex.srows) * nkb, n, full);
-            bulk_g2s(sd + kGRows * nkb, ex.s13 + static_cast<size_t>(u0 / ex.srows) * nkb, n, full);
+      tc::fence_after_sync();
+      const uint32_t bt = smem_u32(smem + S.b + (DOWN ? bb * S.b_bytes : 0));
+      const uint32_t d = tmem + ab * acc_cols;
+      for (int c = 0; c < nchunks; ++c) {
+        if (lane == 0) ready = mbar_wait(&aux.full[stage], full_par);
+        ready = __shfl_sync(0xffffffffu, ready, 0);
+        if (!ready) {
+          if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        if (lane == 0) {
+          const uint32_t a = smem_u32(smem + S.stage + stage * kStageBytes);
+          for (int j = 0; j < 2 && 2 * c + j < nkb; ++j) {
+            const int kb = 2 * c + j;
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4)
+              tc::mma_f8(d + kb * 16, tc::smem_desc(a + j * kSlabBytes + 32 * k4),
+                         tc::smem_desc(bt + kb * kBSlabBytes + 32 * k4), idesc, k4 > 0);
           }
-        } else {
-          const int nkb = p.I / 128;
-          const int n0 = d.b * kDRows;
-          const uint32_t blk = kDRows * p.I;
-          const uint32_t sbytes = ex.sc2_bulk ? (ex.srows == 1 ? kDRows * nkb * 4u : nkb * 4u) : 0u;
-          const uint32_t hbytes = static_cast<uint32_t>(p.T) * p.I * 2;
-          mbar_arrive_expect_tx(full, blk + sbytes + hbytes);
-          bulk_g2s(st, ex.w2 + static_cast<size_t>(n0) * p.I, blk, full);
-          if (ex.sc2_bulk) bulk_g2s(st + S.d_sc, ex.s2 + static_cast<size_t>(n0 / ex.srows) * nkb, sbytes, full);
-          if (waited) bulk_g2s(st + S.d_h, p.ws + L.h + static_cast<size_t>(d.a) * L.h_stride, hbytes, full);
+          tc::mma_commit(&aux.empty[stage]);  // the stage is free once these MMAs have read it
+        }
+        __syncwarp();
+        if (++stage == S.nstages) {
+          stage = 0;
+          full_par ^= 1u;
         }
       }
-      if (DOWN && !waited) pend[npend++] = stage;
+      if (ok && lane == 0) tc::mma_commit(&aux.acc_full[ab]);
       __syncwarp();
-      if (++stage == kStages) {
-        stage = 0;
-        empty_par ^= 1u;
-      }
     }
-    if (!waited) wait_predecessor();
-    // one END per consumer group, in ring order
-    for (int e = 0; e < kGroups; ++e) {
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&misc->empty[stage], empty_par);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (lane == 0) {
-        if (!ok) flag_error(p, L, STATUS_TIMEOUT);
-        misc->desc[stage] = Desc{ITEM_END, 0, 0, 0};
-        mbar_arrive(&misc->full[stage]);
-      }
-      __syncwarp();
-      if (++stage == kStages) {
-        stage = 0;
-        empty_par ^= 1u;
+  } else if (warp < kWarpEpi) {
+    // ================================================================ activation split
+    const int ptid = tid - kWarpSplit * 32;
+    if (!DOWN) {
+      griddep_wait();
+      griddep_launch();
+      split_x(p, smem + S.b, aux, ptid);
+      named_bar(kBarSelect, kThreads);
+      named_bar(kBarTable, kThreads);
+    } else {
+      named_bar(kBarSelect, kThreads);
+      named_bar(kBarTable, kThreads);
+      griddep_wait();  // h comes from the up kernel
+      griddep_launch();
+      const int n_items = aux.n_slots * per_slot;
+      for (int k = 0;; ++k) {
+        const int idx = blockIdx.x + k * gridDim.x;
+        if (idx >= n_items) break;
+        const int bb = k & 1;
+        // one thread waits; the outcome reaches both warps through shared memory and a barrier
+        if (ptid == 0) {
+          aux.split_ok = mbar_wait(&aux.b_free[bb], ((k >> 1) & 1) ^ 1u) ? 1 : 0;
+          if (!aux.split_ok) flag_error(p, L, STATUS_TIMEOUT);
+        }
+        named_bar(kBarSplit, kSplitThreads);
+        if (!aux.split_ok) break;
+        split_h(p, L, smem + S.b + bb * S.b_bytes, aux.hmax[bb], idx / per_slot, ptid);
+        mbar_arrive(&aux.b_ready[bb]);
       }
     }
   } else {
-    // ================================================================ consumers (two groups)
-    const int gid = warp / kGroupWarps, gw = warp % kGroupWarps;
-    const int gtid = tid - gid * kGroupThreads;
-    const int bar_id = 1 + gid;
-    const Group G = group_scratch(smem, S, gid);
-    const uint8_t* xq = smem + S.xq;
-    griddep_wait();
-    griddep_launch();
+    // ================================================================ epilogue (+ route table)
+    const int e = warp - kWarpEpi;  // TMEM lane quarter (warp % 4)
     if (!DOWN) {
-      prepare_x(p, smem + S.xq, misc, warp, lane, S.xp);
-      named_bar(kBarAll, kConsumers);
+      griddep_wait();
+      griddep_launch();
     }
-    int stage = gid;
-    uint32_t full_par = 0;
-    for (;;) {
-      if (!mbar_wait(&misc->full[stage], full_par)) {
+    if (p.mode == 1 && e < p.T) route_row(p, L, e, lane, tab, !DOWN && blockIdx.x == 0);
+    named_bar(kBarSelect, kThreads);
+    if (warp == kWarpEpi) {
+      const int n = p.mode == 1 ? table_from_selection(p, lane, tab) : table_from_ids(p, L, lane, tab, !DOWN);
+      if (lane == 0) aux.n_slots = n;
+    }
+    named_bar(kBarTable, kThreads);
+    if (DOWN) {
+      griddep_wait();
+      griddep_launch();
+      if (blockIdx.x == 0 && warp == kWarpEpi) {
+        // the combine kernel reads the slot count and the shared gate of this call from the workspace
+        if (lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(aux.n_slots);
+        if (lane < p.T) reinterpret_cast<float*>(p.ws + L.coef)[lane] = tab.coef[lane];
+      }
+    }
+    const int n_items = aux.n_slots * per_slot;
+    for (int k = 0;; ++k) {
+      const int idx = blockIdx.x + k * gridDim.x;
+      if (idx >= n_items) break;
+      const int ab = k % nacc, bb = k & 1;
+      bool ready = true;
+      if (lane == 0) {
+        ready = mbar_wait(&aux.acc_full[ab], (k / nacc) & 1);
+        if (ready && DOWN) ready = mbar_wait(&aux.b_ready[bb], (k >> 1) & 1);
+      }
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) {
         if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
         break;
       }
-      const Desc d = misc->desc[stage];
-      if (d.kind == ITEM_END) break;
-      const uint8_t* st = smem + S.stage + stage * S.stage_bytes;
+      tc::fence_after_sync();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * e) << 16) + ab * acc_cols;
       if (!DOWN)
-        consume_g(p, L, S, xq, st, d, misc, G, tab_expert, gw, lane, bar_id);
+        epilogue_up(p, L, aux, taddr, &aux.acc_empty[ab], idx / per_slot, idx % per_slot, e, lane, k);
       else
-        consume_d(p, L, S, st, d, G, tab_coef, tab_expert, gw, lane, gtid, bar_id);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&misc->empty[stage]);
-      stage += kGroups;
-      if (stage >= kStages) {
-        stage -= kStages;
-        full_par ^= 1u;
-      }
+        epilogue_down(p, L, aux, taddr, &aux.acc_empty[ab], &aux.b_free[bb], aux.hmax[bb], idx / per_slot,
+                      idx % per_slot, e, lane);
     }
   }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == kWarpMma) tc::tmem_dealloc(tmem, tmem_cols);
 }
 
 // ------------------------------------------------------------------ combine kernel
@@ -876,13 +945,13 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Params p
   const bool sh = p.sh_w13 != nullptr;
   // the slot count, the shared gate and every slot's partial are requested at once: one L2 round
   // trip; slots past the count hold stale data and are masked
-  const int nb = n / kDRows, r = n % kDRows;
-  const float* col = partial_block(p, L, nb, 0) + t * kDRows + r;
+  const int nb = n / kBlockRows, r = n % kBlockRows;
+  const float* col = partial_block(p, L, nb, 0) + t * kBlockRows + r;
   const uint32_t n_slots = __ldcg(ctrl(p, L) + CTRL_NSLOTS);
   const float gate = sh ? __ldcg(reinterpret_cast<const float*>(p.ws + L.coef) + t) : 0.f;
   float v[kMaxSlots];
 #pragma unroll
-  for (int s = 0; s < kMaxSlots; ++s) v[s] = __ldcg(col + s * kMaxT * kDRows);
+  for (int s = 0; s < kMaxSlots; ++s) v[s] = __ldcg(col + s * kMaxT * kBlockRows);
   float acc = (!sh && n_slots > 0u) ? v[0] : 0.f;
 #pragma unroll
   for (int s = 1; s < kMaxSlots; ++s) acc += static_cast<uint32_t>(s) < n_slots ? v[s] : 0.f;
@@ -902,9 +971,9 @@ size_t moe_ws_bytes(int H, int I) { return moe::ws_layout(H, I).total; }
 
 namespace {
 
-template <typename Kernel>
-int launch_one(Kernel kernel, int grid, int block, size_t smem, cudaStream_t stream, const moe::Params& p,
-               const char* name) {
+template <typename... KArgs, typename... Args>
+int launch_one(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t stream, const char* name,
+               Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(block);
@@ -915,7 +984,7 @@ int launch_one(Kernel kernel, int grid, int block, size_t smem, cudaStream_t str
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, p);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (err != cudaSuccess) {
     set_error(std::string(name) + " launch: " + cudaGetErrorString(err));
     return 2;
@@ -926,7 +995,7 @@ int launch_one(Kernel kernel, int grid, int block, size_t smem, cudaStream_t str
 }  // namespace
 
 int launch_moe(const moe::Params& p, cudaStream_t stream) {
-  const moe::SmemLayout S = moe::smem_layout(p.H, p.I);
+  const moe::SmemLayout su = moe::smem_layout(false, p.H, p.I), sd = moe::smem_layout(true, p.H, p.I);
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     set_error("cudaGetDevice failed");
@@ -954,19 +1023,39 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
     }
     configured[dev] = true;
   }
+  // TMA maps of the expert weights: routed experts [E][2I][H] and [E][H][I] bytes with the caller's
+  // expert strides; the shared expert as a single expert. Up items take 64-row boxes (gate and up
+  // halves), down items 128-row boxes.
+  const uint64_t H = static_cast<uint64_t>(p.H), I = static_cast<uint64_t>(p.I);
+  CUtensorMap m13, m2, msh13, msh2;
+  if (!tensor_map_3d(&m13, p.w13, H, 2 * I, static_cast<uint64_t>(p.n_experts), H, static_cast<uint64_t>(p.w13_stride),
+                     moe::kUpHalf) ||
+      !tensor_map_3d(&m2, p.w2, I, H, static_cast<uint64_t>(p.n_experts), I, static_cast<uint64_t>(p.w2_stride),
+                     moe::kBlockRows))
+    return 2;
+  if (p.sh_w13) {
+    if (!tensor_map_3d(&msh13, p.sh_w13, H, 2 * I, 1, H, 2 * I * H, moe::kUpHalf) ||
+        !tensor_map_3d(&msh2, p.sh_w2, I, H, 1, I, H * I, moe::kBlockRows))
+      return 2;
+  } else {
+    msh13 = m13;
+    msh2 = m2;
+  }
   const int sms = sm_count(dev);
   int launches = 0;
   if (p.mode == 1) {
     const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
     if (int rc = launch_one(moe::route_kernel, (rows + moe::kRouteWarps - 1) / moe::kRouteWarps,
-                            moe::kRouteWarps * 32, 0, stream, p, "moe route"))
+                            moe::kRouteWarps * 32, 0, stream, "moe route", p))
       return rc;
     ++launches;
   }
-  if (int rc = launch_one(moe::expert_kernel<false>, sms, moe::kThreads, S.total, stream, p, "moe up")) return rc;
-  if (int rc = launch_one(moe::expert_kernel<true>, sms, moe::kThreads, S.total, stream, p, "moe down")) return rc;
+  if (int rc = launch_one(moe::expert_kernel<false>, sms, moe::kThreads, su.total, stream, "moe up", p, m13, msh13))
+    return rc;
+  if (int rc = launch_one(moe::expert_kernel<true>, sms, moe::kThreads, sd.total, stream, "moe down", p, m2, msh2))
+    return rc;
   if (int rc = launch_one(moe::combine_kernel, (p.T * p.H + moe::kCombineThreads - 1) / moe::kCombineThreads,
-                          moe::kCombineThreads, 0, stream, p, "moe combine"))
+                          moe::kCombineThreads, 0, stream, "moe combine", p))
     return rc;
   note_launches(launches + 3);
   return 0;
@@ -994,16 +1083,6 @@ int check_common(int T, int H, int I, int top_k, const void* x, const void* w13,
   if (srows != 1 && srows != 128) return set_error("srows must be 1 or 128"), 1;
   if (workspace_bytes < dm3::moe_ws_bytes(H, I)) return set_error("workspace too small"), 4;
   return 0;
-}
-
-// Scale rows are staged by bulk copy when every address and size involved is a 16-byte multiple:
-// 1x128 rows always are (8 or 64 rows of K/128 floats); 128x128 rows need K/128 % 4 == 0.
-void set_bulk_flags(dm3::moe::Params& p, int64_t s13_stride, int64_t s2_stride) {
-  const int nkh = p.H / 128, nki = p.I / 128;
-  p.sc13_bulk = aligned16(p.s13) && (s13_stride * 4) % 16 == 0 && (p.srows == 1 || nkh % 4 == 0);
-  p.sc2_bulk = aligned16(p.s2) && (s2_stride * 4) % 16 == 0 && (p.srows == 1 || nki % 4 == 0);
-  p.sh_sc13_bulk = p.sh_w13 && aligned16(p.sh_s13) && (p.sh_srows == 1 || nkh % 4 == 0);
-  p.sh_sc2_bulk = p.sh_w13 && aligned16(p.sh_s2) && (p.sh_srows == 1 || nki % 4 == 0);
 }
 
 }  // namespace
@@ -1047,7 +1126,6 @@ extern "C" int dm3_moe_forward(const void* x, int T, int H, int I, const int64_t
   p.sh_srows = 128;
   p.y = static_cast<__nv_bfloat16*>(y);
   p.ws = static_cast<uint8_t*>(workspace);
-  set_bulk_flags(p, s13_stride, s2_stride);
   return dm3::launch_moe(p, static_cast<cudaStream_t>(stream));
 }
 
@@ -1106,7 +1184,6 @@ extern "C" int dm3_moe_layer(const void* x, int T, int H, int I, const void* rou
   p.out_bias = out_bias;
   p.y = static_cast<__nv_bfloat16*>(y);
   p.ws = static_cast<uint8_t*>(workspace);
-  set_bulk_flags(p, s13_stride, s2_stride);
   return dm3::launch_moe(p, static_cast<cudaStream_t>(stream));
 }
 
