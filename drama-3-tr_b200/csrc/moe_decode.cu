@@ -41,9 +41,10 @@ namespace dm3 {
 namespace moe {
 
 constexpr int kThreads = 256;       // 8 warps
-constexpr int kWarpTma = 0, kWarpMma = 1, kWarpSplit = 2, kWarpEpi = 4;
-constexpr int kSplitThreads = 64;   // warps 2-3
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpEpi = 4;
+constexpr int kSplitThreads = 192;  // up: every warp but the producer and the table warp (4)
 constexpr int kEpiThreads = 128;    // warps 4-7
+constexpr int kGroup = 32;          // k elements per activation exponent of h (one MMA K step)
 constexpr int kTileRows = 128;      // weight rows per MMA tile (M)
 constexpr int kUpHalf = 64;         // gate rows (and as many up rows) per up item
 constexpr int kBlockRows = 128;     // output rows per down item (= rows per partial block)
@@ -52,12 +53,12 @@ constexpr int kSlabBytes = kTileRows * 128;   // one 128-byte K slab of a weight
 constexpr int kStageBytes = 2 * kSlabBytes;   // two slabs per ring stage
 constexpr int kBSlabBytes = kN * 128;         // one K slab of the activation tile
 constexpr int kUpStages = 5, kDownStages = 6;
-constexpr int kUpAcc = 2, kDownAcc = 4;       // TMEM accumulator buffers
-constexpr uint32_t kUpTmemCols = 512, kDownTmemCols = 256;
+constexpr int kUpAcc = 2, kDownAcc = 2;       // TMEM accumulator buffers
+constexpr uint32_t kUpTmemCols = 512, kDownTmemCols = 512;
 constexpr int kRouteWarps = 4;      // router rows per route CTA (one warp per row)
 constexpr int kCombineThreads = 256;
 // named barriers (0 is __syncthreads)
-constexpr int kBarSelect = 1, kBarTable = 2, kBarSplit = 3;
+constexpr int kBarTable = 1, kBarSplit = 2;
 
 struct Params {
   int T, H, I, top_k;
@@ -96,11 +97,11 @@ struct Params {
 // Control words, the shared gate of the call, the router logits, the bf16 SwiGLU activations h and
 // the fp32 per-slot partial outputs. Offsets do not depend on the row count, so one workspace
 // serves every T of a given (H, I). Nothing in it carries state from one call to the next except
-// the sticky status word.
+// the sticky status word (the route kernel's CTA counter is back at zero after every call).
 struct WsLayout {
-  size_t ctrl, slot_expert, coef, logits, h, h_stride, partial, total;
+  size_t ctrl, slot_expert, coef, logits, himg, himg_stride, hinv, partial, total;
 };
-enum : int { CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
+enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -115,10 +116,15 @@ __host__ __device__ inline WsLayout ws_layout(int H, int I) {
   o += align_up(kMaxSlots * kMaxT * 4, 16);
   L.logits = o;
   o += align_up(kMaxT * (kMaxRouter + 1) * 4, 16);
+  // per slot: h split into e4m3 hi (rows 0-3) and lo (rows 4-7) as the down kernel's activation
+  // tile, 16 rows x I bytes in the swizzled slab layout (rows 8-15 are never written)
+  o = align_up(o, 1024);
+  L.himg_stride = static_cast<size_t>(I / 128) * kBSlabBytes;
+  L.himg = o;
+  o += L.himg_stride * kMaxSlots;
+  L.hinv = o;  // [kMaxSlots][kMaxI / kGroup][kMaxT] fp32: 2^-e of each 32-element group of h
+  o += static_cast<size_t>(kMaxSlots) * (kMaxI / kGroup) * kMaxT * 4;
   o = align_up(o, 128);
-  L.h_stride = align_up(static_cast<size_t>(kMaxT) * I * 2, 128);  // per slot: h[t][I] bf16
-  L.h = o;
-  o += L.h_stride * kMaxSlots;
   L.partial = o;  // [H / 128][kMaxSlots][kMaxT][128] fp32: one output block's slots are adjacent
   o += static_cast<size_t>(H / kBlockRows) * kMaxSlots * kMaxT * kBlockRows * 4;
   L.total = align_up(o, 256);
@@ -134,9 +140,6 @@ __device__ __forceinline__ float* partial_block(const Params& p, const WsLayout&
 struct Table {
   int expert[kMaxSlots];             // routed expert of each slot (slot 0 = shared expert when present)
   float coef[kMaxSlots * kMaxT];     // [slot][row] routing weight (the shared slot: its sigmoid gate)
-  int sel_e[kMaxT * kMaxTopK];       // selected experts of each row, in selection order
-  float sel_w[kMaxT * kMaxTopK];     // their renormalised bf16 weights
-  float shared_coef[kMaxT];
   int kbuf[32];
   float wbuf[32];
 };
@@ -145,13 +148,12 @@ struct Table {
 struct Aux {
   uint64_t full[8], empty[8];        // TMA ring: bytes landed / MMAs done reading
   uint64_t acc_full[4], acc_empty[4];  // TMEM accumulators: MMAs done / epilogue done reading
-  uint64_t b_ready[2], b_free[2];    // activation tiles (down): split written / epilogue done
+  uint64_t b_ready[2], b_free[2];    // activation tiles (down): copied in / MMAs done reading
   uint64_t upv_full, upv_empty;      // up: up-row values written / read
   uint32_t tmem;
-  int split_ok;
   int n_slots;
   float xinv[kMaxT];                 // up: 2^-e of each token's split
-  uint32_t hmax[2][kMaxT];           // down: |h| maxima of each tile's tokens (float bits)
+  uint32_t xmax[kMaxT];              // up: |x| maxima (float bits)
   float upv[kUpHalf][kMaxT];         // up: the up-row values handed to the gate-row threads
   Table tab;
 };
@@ -210,10 +212,10 @@ __device__ __forceinline__ ExpertRef expert_ref(const Params& p, int slot, const
 }
 
 // ------------------------------------------------------------------ route table helpers
-// Builds slots from (token, expert, weight) pairs held one per lane (lanes >= n invalid).
-// Slot order: optional shared expert first, then distinct routed experts ascending. Returns the
-// slot count. One warp; tab.kbuf / tab.wbuf are its scratch.
-__device__ int build_slots(int lane, int n, int t, int e, float w, bool shared, int T, Table& tab) {
+// Builds slots from (token, expert, weight) pairs held one per lane (lanes >= n invalid), for
+// routing given by the caller (any expert count). Slot order: distinct experts ascending. Returns
+// the slot count. One warp; tab.kbuf / tab.wbuf are its scratch.
+__device__ int build_slots(int lane, int n, int t, int e, float w, int T, Table& tab) {
   const bool valid = lane < n && e >= 0;
   const int key = valid ? e : 0x7fffffff;
   tab.kbuf[lane] = key;
@@ -224,7 +226,6 @@ __device__ int build_slots(int lane, int n, int t, int e, float w, bool shared, 
   __syncwarp();
   int rank = 0;  // distinct experts below this one
   for (unsigned f = firsts; f; f &= f - 1u) rank += tab.kbuf[__ffs(f) - 1] < key ? 1 : 0;
-  const int base = shared ? 1 : 0;
   // one writer per (slot, row): a repeated pair (only possible with malformed ids) is summed in lane order
   const int key2 = valid ? ((rank << 3) | t) : -1 - lane;
   const unsigned grp = __match_any_sync(0xffffffffu, key2);
@@ -233,15 +234,12 @@ __device__ int build_slots(int lane, int n, int t, int e, float w, bool shared, 
   if (valid && (__ffs(grp) - 1 == lane)) {
     float wsum = 0.f;
     for (unsigned g = grp; g; g &= g - 1u) wsum += tab.wbuf[__ffs(g) - 1];
-    tab.expert[base + rank] = e;
-    tab.coef[(base + rank) * kMaxT + t] = wsum;
-  }
-  if (shared && lane == 0) {
-    tab.expert[0] = -1;
-    for (int tt = 0; tt < T; ++tt) tab.coef[tt] = tab.shared_coef[tt];
+    tab.expert[rank] = e;
+    tab.coef[rank * kMaxT + t] = wsum;
   }
   __syncwarp();
-  return base + __popc(firsts);
+  (void)T;
+  return __popc(firsts);
 }
 
 // Route table from the caller's ids / weights (routing given), for one warp.
@@ -259,16 +257,30 @@ __device__ int table_from_ids(const Params& p, const WsLayout& L, int lane, Tabl
       flag_error(p, L, STATUS_BAD_EXPERT);
     }
   }
-  return build_slots(lane, n, t, e, w, false, p.T, tab);
+  return build_slots(lane, n, t, e, w, p.T, tab);
 }
 
-// Route table from the row selections route_row left in tab.sel_e / sel_w, for one warp.
-__device__ int table_from_selection(const Params& p, int lane, Table& tab) {
-  const int n = p.T * p.top_k;
-  const int t = lane < n ? lane / p.top_k : 0;
-  const int e = lane < n ? tab.sel_e[lane] : -1;
-  const float w = lane < n ? tab.sel_w[lane] : 0.f;
-  return build_slots(lane, n, t, e, w, p.sh_w13 != nullptr, p.T, tab);
+// Route table the route kernel left in the workspace, for one warp (one L2 round trip).
+__device__ int table_from_ws(const Params& p, const WsLayout& L, int lane, Table& tab) {
+  constexpr int kE = (kMaxSlots + 31) / 32, kC = (kMaxSlots * kMaxT + 31) / 32;
+  const int* gse = reinterpret_cast<const int*>(p.ws + L.slot_expert);
+  const float* gco = reinterpret_cast<const float*>(p.ws + L.coef);
+  // every load is issued before the first use: one L2 round trip
+  const uint32_t n_slots = __ldcg(ctrl(p, L) + CTRL_NSLOTS);
+  int ev[kE];
+  float cv[kC];
+#pragma unroll
+  for (int q = 0; q < kE; ++q) ev[q] = lane + 32 * q < kMaxSlots ? __ldcg(gse + lane + 32 * q) : 0;
+#pragma unroll
+  for (int q = 0; q < kC; ++q) cv[q] = lane + 32 * q < kMaxSlots * kMaxT ? __ldcg(gco + lane + 32 * q) : 0.f;
+#pragma unroll
+  for (int q = 0; q < kE; ++q)
+    if (lane + 32 * q < kMaxSlots) tab.expert[lane + 32 * q] = ev[q];
+#pragma unroll
+  for (int q = 0; q < kC; ++q)
+    if (lane + 32 * q < kMaxSlots * kMaxT) tab.coef[lane + 32 * q] = cv[q];
+  __syncwarp();
+  return static_cast<int>(n_slots);
 }
 
 // ------------------------------------------------------------------ route kernel
@@ -281,64 +293,189 @@ __device__ __forceinline__ float key_value(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-// Top-k of row t by one warp from the route kernel's logits, and the renormalised weights, into
-// tab.sel_e / sel_w / shared_coef. Mirrors Speaker.__call__ (engine.py:233-235):
-// probs = softmax(logits), (w, ids) = probs.topk(k), w = (w / w.sum()).to(bf16). Selection uses the
-// logits themselves (softmax is monotonic), ties to the lower index; each step is one warp-wide
-// max of the lanes' best keys and one min of the expert indices that hold it.
-__device__ void route_row(const Params& p, const WsLayout& L, int t, int lane, Table& tab, bool write_out) {
-  const int E = p.n_router, K = p.top_k;
-  const float* lg = reinterpret_cast<const float*>(p.ws + L.logits) + t * (kMaxRouter + 1);
-  float lv[kMaxRouter / 32];
-  uint32_t key[kMaxRouter / 32];
+__device__ __forceinline__ void cswap_desc(uint64_t& a, uint64_t& b) {
+  const uint64_t hi = a > b ? a : b, lo = a > b ? b : a;
+  a = hi;
+  b = lo;
+}
+
+// The 8 largest of 256 packed keys held 8 per lane, sorted descending; every lane ends with the
+// same 8. Each lane sorts its own 8 (Batcher's 19-comparator network), then five butterfly rounds
+// merge with the partner lane's list: the elementwise max of one list and the other reversed is
+// the top 8 of both as a bitonic sequence, which three half-cleaner stages sort again.
+__device__ __forceinline__ void warp_top8(uint64_t (&k)[8]) {
+  cswap_desc(k[0], k[1]); cswap_desc(k[2], k[3]); cswap_desc(k[4], k[5]); cswap_desc(k[6], k[7]);
+  cswap_desc(k[0], k[2]); cswap_desc(k[1], k[3]); cswap_desc(k[4], k[6]); cswap_desc(k[5], k[7]);
+  cswap_desc(k[1], k[2]); cswap_desc(k[5], k[6]);
+  cswap_desc(k[0], k[4]); cswap_desc(k[1], k[5]); cswap_desc(k[2], k[6]); cswap_desc(k[3], k[7]);
+  cswap_desc(k[2], k[4]); cswap_desc(k[3], k[5]);
+  cswap_desc(k[1], k[2]); cswap_desc(k[3], k[4]); cswap_desc(k[5], k[6]);
 #pragma unroll
-  for (int i = 0; i < kMaxRouter / 32; ++i) lv[i] = lane + 32 * i < E ? __ldcg(lg + lane + 32 * i) : -FLT_MAX;
-  const float gl = (lane == 0 && p.sh_gate) ? __ldcg(lg + E) : 0.f;
-  uint32_t kmax = 0u;
+  for (int d = 1; d < 32; d <<= 1) {
+    uint64_t o[8];
 #pragma unroll
-  for (int i = 0; i < kMaxRouter / 32; ++i) {
-    key[i] = lane + 32 * i < E ? order_key(lv[i]) : 0u;
-    kmax = max(kmax, key[i]);
+    for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xffffffffu, k[i], d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) k[i] = k[i] > o[7 - i] ? k[i] : o[7 - i];
+    cswap_desc(k[0], k[4]); cswap_desc(k[1], k[5]); cswap_desc(k[2], k[6]); cswap_desc(k[3], k[7]);
+    cswap_desc(k[0], k[2]); cswap_desc(k[1], k[3]); cswap_desc(k[4], k[6]); cswap_desc(k[5], k[7]);
+    cswap_desc(k[0], k[1]); cswap_desc(k[2], k[3]); cswap_desc(k[4], k[5]); cswap_desc(k[6], k[7]);
   }
-  const float m = key_value(__reduce_max_sync(0xffffffffu, kmax));
+}
+
+// Shared-memory tail of the route kernel: the logits of every row (the last column is the shared
+// expert's gate), the selections and the table scratch of the last CTA.
+struct RouteTail {
+  float logits[kMaxT][kMaxRouter + 1];
+  int sel_e[kMaxT * kMaxTopK];
+  float sel_w[kMaxT * kMaxTopK];
+  float shared_coef[kMaxT];
+  uint32_t bitmap[kMaxRouter / 32];
+  uint64_t bar;
+  int last;
+};
+
+__device__ __forceinline__ void cswap_desc32(uint32_t& a, uint32_t& b) {
+  const uint32_t hi = max(a, b), lo = min(a, b);
+  a = hi;
+  b = lo;
+}
+
+// warp_top8 for 32-bit keys (same network and merge rounds).
+__device__ __forceinline__ void warp_top8_32(uint32_t (&k)[8]) {
+  cswap_desc32(k[0], k[1]); cswap_desc32(k[2], k[3]); cswap_desc32(k[4], k[5]); cswap_desc32(k[6], k[7]);
+  cswap_desc32(k[0], k[2]); cswap_desc32(k[1], k[3]); cswap_desc32(k[4], k[6]); cswap_desc32(k[5], k[7]);
+  cswap_desc32(k[1], k[2]); cswap_desc32(k[5], k[6]);
+  cswap_desc32(k[0], k[4]); cswap_desc32(k[1], k[5]); cswap_desc32(k[2], k[6]); cswap_desc32(k[3], k[7]);
+  cswap_desc32(k[2], k[4]); cswap_desc32(k[3], k[5]);
+  cswap_desc32(k[1], k[2]); cswap_desc32(k[3], k[4]); cswap_desc32(k[5], k[6]);
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xffffffffu, k[i], d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) k[i] = max(k[i], o[7 - i]);
+    cswap_desc32(k[0], k[4]); cswap_desc32(k[1], k[5]); cswap_desc32(k[2], k[6]); cswap_desc32(k[3], k[7]);
+    cswap_desc32(k[0], k[2]); cswap_desc32(k[1], k[3]); cswap_desc32(k[4], k[6]); cswap_desc32(k[5], k[7]);
+    cswap_desc32(k[0], k[1]); cswap_desc32(k[2], k[3]); cswap_desc32(k[4], k[5]); cswap_desc32(k[6], k[7]);
+  }
+}
+
+// Top-k of row t by one warp from the logits in shared memory. Mirrors Speaker.__call__
+// (engine.py:233-235): probs = softmax(logits), (w, ids) = probs.topk(k),
+// w = (w / w.sum()).to(bf16). Selection uses the logits themselves (softmax is monotonic) with
+// ties to the lower index: keys pack (logit order, ~index) so one comparison decides both. When
+// every logit is a bf16 value (bf16 logits without a bias) the order fits 16 bits and a key is
+// 32 bits; otherwise 64.
+__device__ void route_row(const Params& p, RouteTail& rt, int t, int lane) {
+  const int E = p.n_router, K = p.top_k;
+  float lv[8];
+  float mloc = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    lv[i] = lane + 32 * i < E ? rt.logits[t][lane + 32 * i] : -FLT_MAX;
+    mloc = fmaxf(mloc, lv[i]);
+  }
+  int sel_e[8];
+  float sel_v[8];
+  if (p.logits_bf16 && p.logit_bias == nullptr) {
+    uint32_t k[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      k[i] = e < E ? ((order_key(lv[i]) >> 16) << 16) | static_cast<uint32_t>(0xFFFF - e) : 0u;
+    }
+    warp_top8_32(k);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sel_e[j] = 0xFFFF - static_cast<int>(k[j] & 0xFFFFu);
+      // the low half of a bf16 value's float bits is zero, which the key inverts for negative values
+      sel_v[j] = key_value((k[j] & 0x80000000u) ? (k[j] & 0xFFFF0000u) : (k[j] | 0x0000FFFFu));
+    }
+  } else {
+    uint64_t k[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      k[i] = e < E ? (static_cast<uint64_t>(order_key(lv[i])) << 32) | static_cast<uint32_t>(~e) : 0ull;
+    }
+    warp_top8(k);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sel_e[j] = static_cast<int>(~static_cast<uint32_t>(k[j]));
+      sel_v[j] = key_value(static_cast<uint32_t>(k[j] >> 32));
+    }
+  }
+  // softmax denominator (the maximum by its own butterfly, so it overlaps the selection)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
+  const float m = mloc;
   float z = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxRouter / 32; ++i)
+  for (int i = 0; i < 8; ++i)
     if (lane + 32 * i < E) z += expf(lv[i] - m);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
-  unsigned taken = 0u;
-  int my_e = -1;
+  // lane j < K: probability of the j-th selection; the sum runs in selection order
+  int my_e = 0;
   float my_v = 0.f;
-  for (int j = 0; j < K; ++j) {
-    uint32_t bk = 0u;
-    int bi = 0;
 #pragma unroll
-    for (int i = 0; i < kMaxRouter / 32; ++i)
-      if (!((taken >> i) & 1u) && key[i] > bk) {
-        bk = key[i];
-        bi = i;
-      }
-    const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
-    const uint32_t cand = (bk == mk && bk != 0u) ? static_cast<uint32_t>(lane + 32 * bi) : 0xffffffffu;
-    const uint32_t be = __reduce_min_sync(0xffffffffu, cand);
-    if (static_cast<int>(be & 31u) == lane) taken |= 1u << (be >> 5);
+  for (int j = 0; j < 8; ++j)
     if (lane == j) {
-      my_e = static_cast<int>(be);
-      my_v = key_value(mk);
+      my_e = sel_e[j];
+      my_v = sel_v[j];
     }
-  }
-  const float my_p = lane < K ? expf(my_v - m) / z : 0.f;
+  const float my_p = expf(my_v - m) / z;
   float psum = 0.f;
-  for (int j = 0; j < K; ++j) psum += __shfl_sync(0xffffffffu, my_p, j);
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    const float pj = __shfl_sync(0xffffffffu, my_p, j);
+    if (j < K) psum += pj;
+  }
   if (lane < K) {
     const __nv_bfloat16 wb = __float2bfloat16_rn(my_p / psum);
-    tab.sel_e[t * K + lane] = my_e;
-    tab.sel_w[t * K + lane] = __bfloat162float(wb);
-    if (write_out && p.ids_out) p.ids_out[t * K + lane] = my_e;
-    if (write_out && p.w_out) p.w_out[t * K + lane] = wb;
+    rt.sel_e[t * K + lane] = my_e;
+    rt.sel_w[t * K + lane] = __bfloat162float(wb);
+    if (p.ids_out) p.ids_out[t * K + lane] = my_e;
+    if (p.w_out) p.w_out[t * K + lane] = wb;
   }
-  if (lane == 0) tab.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-gl))) : 1.f;
+  if (lane == 0) rt.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-rt.logits[t][E]))) : 1.f;
+}
+
+// The route table of the call from the selections, by one warp, into the workspace: slot 0 is the
+// shared expert when present, then the distinct routed experts ascending (rank = count of selected
+// experts below, from a bitmap of the router's experts).
+__device__ void write_table(const Params& p, const WsLayout& L, RouteTail& rt, int lane) {
+  const int n = p.T * p.top_k;
+  const bool valid = lane < n;
+  const int e = valid ? rt.sel_e[lane] : 0;
+  const int t = valid ? lane / p.top_k : 0;
+  if (lane < kMaxRouter / 32) rt.bitmap[lane] = 0u;
+  __syncwarp();
+  if (valid) atomicOr(&rt.bitmap[e >> 5], 1u << (e & 31));
+  __syncwarp();
+  int rank = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kMaxRouter / 32; ++w) {
+    const uint32_t word = rt.bitmap[w];
+    total += __popc(word);
+    if (w < (e >> 5)) rank += __popc(word);
+  }
+  rank += __popc(rt.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
+  const bool sh = p.sh_w13 != nullptr;
+  const int base = sh ? 1 : 0;
+  int* gse = reinterpret_cast<int*>(p.ws + L.slot_expert);
+  float* gco = reinterpret_cast<float*>(p.ws + L.coef);
+  for (int i = lane; i < kMaxSlots * kMaxT; i += 32) gco[i] = 0.f;
+  __syncwarp();
+  if (valid) {
+    gse[base + rank] = e;  // rows that chose the same expert write the same value
+    gco[(base + rank) * kMaxT + t] = rt.sel_w[lane];
+  }
+  if (sh && lane < p.T) gco[lane] = rt.shared_coef[lane];
+  if (sh && lane == 0) gse[0] = -1;
+  if (lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(base + total);
 }
 
 // Adds a to the unevaluated sum hi + lo without rounding error in hi (Knuth's TwoSum; the error
@@ -350,105 +487,143 @@ __device__ __forceinline__ void two_sum_acc(float& hi, float& lo, float a) {
   hi = s;
 }
 
-// Router logits: one warp per router row (plus the shared expert's gate row). The row is fetched
-// into registers before griddepcontrol.wait (router weights never depend on the preceding kernel);
-// the activation rows are staged in shared memory after it, all loads in flight at once. Every
-// product is exact in fp32 (bf16 x bf16; bf16 x fp32 keeps its rounding error through an fma) and
-// is summed as a hi + lo pair, which carries about 48 significant bits, so the logit is the sum
-// rounded once to fp32 (then to bf16 for a bf16 router), + the optional logit bias. The shared gate
-// row is rounded to bf16 as a bf16 linear's output. The top-k runs in the kernels that use it.
-__global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const Params p) {
+// Shared memory of the route kernel: the CTA's router rows (staged by bulk copies before the
+// wait), the activation rows, then RouteTail.
+__host__ __device__ inline size_t route_tail_offset(int H, bool w32) {
+  return align_up(static_cast<size_t>(kRouteWarps) * H * (w32 ? 4 : 2) + static_cast<size_t>(kMaxT) * H * 2, 16);
+}
+__host__ __device__ inline size_t route_smem_bytes(int H, bool w32) {
+  return route_tail_offset(H, w32) + align_up(sizeof(RouteTail), 16);
+}
+
+// Router logits, then the route table. One warp per router row (plus the shared expert's gate
+// row). The CTA's rows are copied into shared memory by the bulk-copy engine before
+// griddepcontrol.wait (router weights never depend on the preceding kernel); the activation rows
+// are staged after it. Every product is exact in fp32 (bf16 x bf16; bf16 x fp32 keeps its rounding
+// error through an fma) and is summed as a hi + lo pair, which carries about 48 significant bits,
+// so the logit is the sum rounded once to fp32 (then to bf16 for a bf16 router), + the optional
+// logit bias. The shared gate row is rounded to bf16 as a bf16 linear's output. The last CTA to
+// finish (one gpu-scope fence per CTA, with no copies in flight) selects the experts of every row
+// (one warp per row) and writes the table.
+template <bool W32>
+__global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) uint8_t rsm[];
   const WsLayout L = ws_layout(p.H, p.I);
-  __shared__ __align__(16) __nv_bfloat16 xs[kMaxT * kMaxH];
+  const int H = p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool sh_gate_row = p.sh_w13 != nullptr && p.sh_gate != nullptr;
   const int rows = p.n_router + (sh_gate_row ? 1 : 0);
-  const int row = blockIdx.x * kRouteWarps + warp;
-  const bool is_router = row < p.n_router;
-  const bool row_f32 = is_router && !p.router_bf16;
-  // this lane's slice of the row: bf16 elements lane*8 + 256*j, or fp32 elements lane*4 + 128*j
-  constexpr int kMaxChunks = kMaxH * 4 / (32 * 16);  // 16-byte chunks per lane of an fp32 row of kMaxH
-  uint4 wv[kMaxChunks];
-  const int chunks = row_f32 ? p.H / 128 : p.H / 256;
-  if (row < rows) {
-    const uint4* src = row_f32 ? reinterpret_cast<const uint4*>(static_cast<const float*>(p.router_w) +
-                                                               static_cast<size_t>(row) * p.H)
-                     : is_router ? reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.router_w) +
-                                                                 static_cast<size_t>(row) * p.H)
-                                 : reinterpret_cast<const uint4*>(p.sh_gate);
-#pragma unroll
-    for (int j = 0; j < kMaxChunks; ++j) wv[j] = j < chunks ? __ldg(src + lane + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
+  const int row0 = blockIdx.x * kRouteWarps;
+  const int row = row0 + warp;
+  const int wsz = W32 ? 4 : 2;
+  uint8_t* wrows = rsm;  // [kRouteWarps][H] weights
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm + static_cast<size_t>(kRouteWarps) * H * wsz);
+  RouteTail& rt = *reinterpret_cast<RouteTail*>(rsm + route_tail_offset(H, W32));
+  if (threadIdx.x == 0) {
+    mbar_init(&rt.bar, 1);
+    fence_mbar_init();
+    uint32_t bytes = 0;
+    for (int r = row0; r < min(rows, row0 + kRouteWarps); ++r) bytes += r < p.n_router ? H * wsz : H * 2;
+    mbar_arrive_expect_tx(&rt.bar, bytes);
+    for (int r = row0; r < min(rows, row0 + kRouteWarps); ++r) {
+      if (r < p.n_router)
+        bulk_g2s(wrows + static_cast<size_t>(r - row0) * H * wsz,
+                 static_cast<const uint8_t*>(p.router_w) + static_cast<size_t>(r) * H * wsz, H * wsz, &rt.bar);
+      else
+        bulk_g2s(wrows + static_cast<size_t>(r - row0) * H * wsz, p.sh_gate, H * 2, &rt.bar);
+    }
   }
   griddep_wait();
   griddep_launch();
-  {
-    constexpr int kPerThread = kMaxT * kMaxH / 8 / (kRouteWarps * 32);
-    const int n16 = p.T * p.H / 8;
-    const uint4* xsrc = reinterpret_cast<const uint4*>(p.x);
-    uint4 v[kPerThread];
+  const uint4* xsrc = reinterpret_cast<const uint4*>(p.x);
+  for (int c = threadIdx.x; c < p.T * H / 8; c += kRouteWarps * 32) reinterpret_cast<uint4*>(xs)[c] = xsrc[c];
+  if (threadIdx.x == 0 && !mbar_wait(&rt.bar, 0)) flag_error(p, L, STATUS_TIMEOUT);
+  __syncthreads();
+  float* logits = reinterpret_cast<float*>(p.ws + L.logits);
+  if (row < rows) {
+    const bool is_router = row < p.n_router;
+    const bool row_w32 = W32 && is_router;  // the shared gate row is bf16 in either case
+    const uint8_t* wr = wrows + static_cast<size_t>(warp) * H * wsz;
+    for (int t = 0; t < p.T; ++t) {
+      const __nv_bfloat16* xr = xs + t * H;
+      float hi[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, lo[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int k = lane * 8; k < H; k += 256) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+        const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+        float w[8];
+        if (row_w32) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(wr + k * 4), w1 = *reinterpret_cast<const uint4*>(wr + k * 4 + 16);
+          w[0] = __uint_as_float(w0.x), w[1] = __uint_as_float(w0.y), w[2] = __uint_as_float(w0.z), w[3] = __uint_as_float(w0.w);
+          w[4] = __uint_as_float(w1.x), w[5] = __uint_as_float(w1.y), w[6] = __uint_as_float(w1.z), w[7] = __uint_as_float(w1.w);
+        } else {
+          const uint4 wv = *reinterpret_cast<const uint4*>(wr + k * 2);
+          const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
 #pragma unroll
-    for (int i = 0; i < kPerThread; ++i) {
-      const int c = threadIdx.x + i * kRouteWarps * 32;
-      v[i] = c < n16 ? xsrc[c] : make_uint4(0u, 0u, 0u, 0u);
-    }
+          for (int i = 0; i < 8; ++i) w[i] = __bfloat162float(we[i]);
+        }
 #pragma unroll
-    for (int i = 0; i < kPerThread; ++i) {
-      const int c = threadIdx.x + i * kRouteWarps * 32;
-      if (c < n16) reinterpret_cast<uint4*>(xs)[c] = v[i];
+        for (int i = 0; i < 8; ++i) {
+          const float xf = __bfloat162float(xe[i]);
+          const float pr = xf * w[i];
+          if (W32) lo[i] += fmaf(xf, w[i], -pr);  // the product's rounding error, exact (0 for bf16 x bf16)
+          two_sum_acc(hi[i], lo[i], pr);
+        }
+      }
+      float h = hi[0], l = lo[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) {
+        l += lo[i];
+        two_sum_acc(h, l, hi[i]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float oh = __shfl_xor_sync(0xffffffffu, h, o);
+        l += __shfl_xor_sync(0xffffffffu, l, o);
+        two_sum_acc(h, l, oh);
+      }
+      if (lane == 0) {
+        float v = h + l;
+        if (is_router) {
+          if (p.logits_bf16) v = bf16_round(v);
+          if (p.logit_bias) v += p.logit_bias[row];
+        } else {
+          v = bf16_round(v);
+        }
+        logits[t * (kMaxRouter + 1) + row] = v;
+      }
     }
   }
   __syncthreads();
-  if (row >= rows) return;
-  float* logits = reinterpret_cast<float*>(p.ws + L.logits);
-  for (int t = 0; t < p.T; ++t) {
-    const __nv_bfloat16* xr = xs + t * p.H;
-    float hi[4] = {0.f, 0.f, 0.f, 0.f}, lo[4] = {0.f, 0.f, 0.f, 0.f};
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t old = atomicAdd(ctrl(p, L) + CTRL_ROUTE_COUNT, 1u);
+    rt.last = old == gridDim.x - 1;
+    if (rt.last) __threadfence();
+  }
+  __syncthreads();
+  if (!rt.last) return;
+  // last CTA: every logit is visible
+  {
+    constexpr int kPer = (kMaxT * (kMaxRouter + 1) + kRouteWarps * 32 - 1) / (kRouteWarps * 32);
+    float v[kPer];
 #pragma unroll
-    for (int j = 0; j < kMaxChunks; ++j) {
-      if (j < chunks) {
-        if (row_f32) {
-          const float* w = reinterpret_cast<const float*>(&wv[j]);
-          const uint2 xv = *reinterpret_cast<const uint2*>(xr + lane * 4 + 128 * j);
-          const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float xf = __bfloat162float(xe[i]);
-            const float pr = xf * w[i];
-            lo[i] += fmaf(xf, w[i], -pr);  // the product's rounding error, exact
-            two_sum_acc(hi[i], lo[i], pr);
-          }
-        } else {
-          const __nv_bfloat16* w = reinterpret_cast<const __nv_bfloat16*>(&wv[j]);
-          const uint4 xv = *reinterpret_cast<const uint4*>(xr + lane * 8 + 256 * j);
-          const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            two_sum_acc(hi[i & 3], lo[i & 3], __bfloat162float(xe[i]) * __bfloat162float(w[i]));
-        }
-      }
-    }
-    float h = hi[0], l = lo[0];
-#pragma unroll
-    for (int i = 1; i < 4; ++i) {
-      l += lo[i];
-      two_sum_acc(h, l, hi[i]);
+    for (int q = 0; q < kPer; ++q) {
+      const int i = threadIdx.x + q * kRouteWarps * 32;
+      v[q] = i < p.T * (kMaxRouter + 1) && i % (kMaxRouter + 1) < rows ? __ldcg(logits + i) : 0.f;
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float oh = __shfl_xor_sync(0xffffffffu, h, o);
-      l += __shfl_xor_sync(0xffffffffu, l, o);
-      two_sum_acc(h, l, oh);
+    for (int q = 0; q < kPer; ++q) {
+      const int i = threadIdx.x + q * kRouteWarps * 32;
+      if (i < kMaxT * (kMaxRouter + 1)) (&rt.logits[0][0])[i] = v[q];
     }
-    if (lane == 0) {
-      float v = h + l;
-      if (is_router) {
-        if (p.logits_bf16) v = bf16_round(v);
-        if (p.logit_bias) v += p.logit_bias[row];
-      } else {
-        v = bf16_round(v);
-      }
-      logits[t * (kMaxRouter + 1) + row] = v;
-    }
+  }
+  __syncthreads();
+  if (warp < p.T) route_row(p, rt, warp, lane);
+  __syncthreads();
+  if (warp == 0) {
+    write_table(p, L, rt, lane);
+    if (lane == 0) ctrl(p, L)[CTRL_ROUTE_COUNT] = 0u;  // every CTA has counted: ready for the next call
   }
 }
 
@@ -478,72 +653,39 @@ __device__ __forceinline__ float abs_max16(const uint4 (&v)[2]) {
 }
 
 // Up: the activation tile of all H. Row t holds the e4m3 hi part of x[t] * 2^e_t (e_t maps the
-// row's absolute maximum into [128, 256)), row 4 + t the lo remainder, every other row zero.
-// Run by the 64 split threads; they fence their writes for the tensor core.
-__device__ void split_x(const Params& p, uint8_t* bt, Aux& aux, int ptid) {
-  const int H = p.H, wl = ptid >> 5, lane = ptid & 31;
-  for (int t = wl; t < p.T; t += 2) {
-    const __nv_bfloat16* xr = p.x + static_cast<size_t>(t) * H;
-    float amax = 0.f;
-    for (int k = lane * 8; k < H; k += 256) {
-      const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(e[i])));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (lane == 0) {
-      aux.hmax[0][t] = __float_as_uint(amax);
-      aux.xinv[t] = exp2i(-split_exponent(amax));
-    }
-  }
+// row's absolute maximum into [128, 256)), row 4 + t the lo remainder. Rows of absent tokens and
+// rows 8-15 only feed accumulator columns that nothing reads, so they are left as they are. Run by
+// the kSplitThreads split threads; every load is issued before the first use, and the threads
+// fence their writes for the tensor core.
+__device__ void split_x(const Params& p, uint8_t* bt, Aux& aux, int sidx) {
+  const int H = p.H, chunks = H / 16, n = p.T * chunks;
+  constexpr int kMaxTasks = (kMaxT * (kMaxH / 16) + kSplitThreads - 1) / kSplitThreads;
+  if (sidx < kMaxT) aux.xmax[sidx] = 0u;
   named_bar(kBarSplit, kSplitThreads);
-  const int chunks = H / 16;
-  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-  for (int task = ptid; task < kMaxT * chunks; task += kSplitThreads) {
-    const int t = task / chunks, c = task % chunks;
-    uint4 hi = z, lo = z;
-    if (t < p.T) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * H + c * 16);
-      const uint4 v[2] = {src[0], src[1]};
-      split16(v, exp2i(split_exponent(__uint_as_float(aux.hmax[0][t]))), hi, lo);
-    }
-    *reinterpret_cast<uint4*>(bt + tc::swz_offset(t, c * 16, kN)) = hi;
-    *reinterpret_cast<uint4*>(bt + tc::swz_offset(4 + t, c * 16, kN)) = lo;
-  }
-  for (int i = ptid; i < (H / 128) * 64; i += kSplitThreads)  // rows 8-15 of every slab
-    *reinterpret_cast<uint4*>(bt + (i / 64) * kBSlabBytes + 1024 + (i % 64) * 16) = z;
-  tc::fence_proxy_async_smem();
-}
-
-// Down: the activation tile of one slot's h (rows t < T; the zero rows are written once per
-// kernel). hmax receives each row's absolute maximum for the epilogue.
-__device__ void split_h(const Params& p, const WsLayout& L, uint8_t* bt, uint32_t* hmax, int slot, int ptid) {
-  const int I = p.I, chunks = I / 16, n = p.T * chunks;
-  constexpr int kMaxTasks = kMaxT * kMaxI / 16 / kSplitThreads;
-  if (ptid < kMaxT) hmax[ptid] = 0u;
-  named_bar(kBarSplit, kSplitThreads);
-  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(p.ws + L.h + static_cast<size_t>(slot) * L.h_stride);
   uint4 v[kMaxTasks][2];
 #pragma unroll
   for (int q = 0; q < kMaxTasks; ++q) {
-    const int task = ptid + q * kSplitThreads;
+    const int task = sidx + q * kSplitThreads;
     if (task < n) {
-      const uint4* src = reinterpret_cast<const uint4*>(h + (task / chunks) * I + (task % chunks) * 16);
-      v[q][0] = __ldcg(src);
-      v[q][1] = __ldcg(src + 1);
-      atomicMax(&hmax[task / chunks], __float_as_uint(abs_max16(v[q])));
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(task / chunks) * H + (task % chunks) * 16);
+      v[q][0] = src[0];
+      v[q][1] = src[1];
     }
   }
-  named_bar(kBarSplit, kSplitThreads);
 #pragma unroll
   for (int q = 0; q < kMaxTasks; ++q) {
-    const int task = ptid + q * kSplitThreads;
+    const int task = sidx + q * kSplitThreads;
+    if (task < n) atomicMax(&aux.xmax[task / chunks], __float_as_uint(abs_max16(v[q])));
+  }
+  named_bar(kBarSplit, kSplitThreads);
+  if (sidx < kMaxT) aux.xinv[sidx] = exp2i(-split_exponent(__uint_as_float(aux.xmax[sidx])));
+#pragma unroll
+  for (int q = 0; q < kMaxTasks; ++q) {
+    const int task = sidx + q * kSplitThreads;
     if (task < n) {
       const int t = task / chunks, c = task % chunks;
       uint4 hi, lo;
-      split16(v[q], exp2i(split_exponent(__uint_as_float(hmax[t]))), hi, lo);
+      split16(v[q], exp2i(split_exponent(__uint_as_float(aux.xmax[t]))), hi, lo);
       *reinterpret_cast<uint4*>(bt + tc::swz_offset(t, c * 16, kN)) = hi;
       *reinterpret_cast<uint4*>(bt + tc::swz_offset(4 + t, c * 16, kN)) = lo;
     }
@@ -552,44 +694,47 @@ __device__ void split_h(const Params& p, const WsLayout& L, uint8_t* bt, uint32_
 }
 
 // ------------------------------------------------------------------ epilogues
-// Sum over k blocks of scale x (hi + lo) for this thread's weight row, from nkb accumulators of
-// 16 TMEM columns each starting at column `col`.
-template <int MaxKb>
-__device__ __forceinline__ void reduce_kblocks(uint32_t taddr, int nkb, const float* sc, float (&acc)[kMaxT]) {
+// Sum over accumulators (16 TMEM columns each, starting at the thread's lane address) of
+// scale x (hi + lo) for this thread's weight row; scale(j) is the accumulator's combined scale.
+template <int MaxAcc, typename ScaleFn>
+__device__ __forceinline__ void reduce_acc(uint32_t taddr, int nacc, ScaleFn scale, float (&acc)[kMaxT]) {
 #pragma unroll
   for (int t = 0; t < kMaxT; ++t) acc[t] = 0.f;
 #pragma unroll
-  for (int kb0 = 0; kb0 < MaxKb; kb0 += 8) {
-    if (kb0 < nkb) {
+  for (int j0 = 0; j0 < MaxAcc; j0 += 8) {
+    if (j0 < nacc) {
       float v[8][8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (kb0 + j < nkb) tc::tmem_ld8(taddr + (kb0 + j) * 16, v[j]);
+        if (j0 + j < nacc) tc::tmem_ld8(taddr + (j0 + j) * 16, v[j]);
       tc::tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        if (kb0 + j < nkb)
+        if (j0 + j < nacc)
 #pragma unroll
-          for (int t = 0; t < kMaxT; ++t) acc[t] = fmaf(sc[kb0 + j], v[j][t] + v[j][4 + t], acc[t]);
+          for (int t = 0; t < kMaxT; ++t) acc[t] = fmaf(scale(j0 + j, t), v[j][t] + v[j][4 + t], acc[t]);
     }
   }
 }
 
+// The block scales of this thread's weight row (issued before the accumulator wait).
+__device__ __forceinline__ void load_scales(const float* srow, int nkb, float* sc, int max_kb) {
+#pragma unroll
+  for (int kb = 0; kb < max_kb; ++kb) sc[kb] = kb < nkb ? __ldg(srow + kb) : 0.f;
+}
+
 // Up: thread r holds gate row 64*blk + r (r < 64) or up row I + 64*blk + r - 64; the up values go
-// through shared memory to the gate threads, which apply SwiGLU and store h. Releases the
-// accumulator buffer (acc_empty) as soon as it has been read.
+// through shared memory to the gate threads, which apply SwiGLU, round h to bf16 (the reference's
+// activation dtype) and write it straight into the down kernel's activation tile: each warp's 32
+// values of a token form one group whose power-of-two scale maps its absolute maximum into
+// [128, 256), and h * 2^e splits exactly into e4m3 hi + lo. Releases the accumulator buffer
+// (acc_empty) as soon as it has been read.
 __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32_t taddr, uint64_t* acc_empty,
-                            int slot, int blk, int e, int lane, int k) {
+                            int slot, int blk, int e, int lane, int k, const float (&sc)[kMaxH / 128]) {
   const int r = 32 * e + lane;
   const int nkb = p.H / 128;
-  const ExpertRef ex = expert_ref(p, slot, aux.tab.expert);
-  const int wrow = r < kUpHalf ? kUpHalf * blk + r : p.I + kUpHalf * blk + (r - kUpHalf);
-  const float* srow = ex.s13 + static_cast<size_t>(wrow / ex.srows) * nkb;
-  float sc[kMaxH / 128];
-#pragma unroll
-  for (int kb = 0; kb < kMaxH / 128; ++kb) sc[kb] = kb < nkb ? __ldg(srow + kb) : 0.f;
   float acc[kMaxT];
-  reduce_kblocks<kMaxH / 128>(taddr, nkb, sc, acc);
+  reduce_acc<kMaxH / 128>(taddr, nkb, [&](int j, int) { return sc[j]; }, acc);
   tc::fence_before_sync();
   __syncwarp();
   if (lane == 0) mbar_arrive(acc_empty);
@@ -613,55 +758,87 @@ __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32
     if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
     return;
   }
-  {
-    const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
-    __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.ws + L.h + static_cast<size_t>(slot) * L.h_stride);
-    for (int t = 0; t < p.T; ++t) {
+  const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
+  float hb[kMaxT], am[kMaxT];
+#pragma unroll
+  for (int t = 0; t < kMaxT; ++t) {
+    hb[t] = 0.f;
+    if (t < p.T) {
+      // silu(g) = g * 1 / (1 + e^-g) with the fast exponential and an IEEE reciprocal; h is rounded
+      // to bf16 right after, far above their error
       float gt = acc[t] * aux.xinv[t];
       float ut = aux.upv[r][t];
-      float hv;
       if (shared_slot) {
         // the shared expert is a chain of bf16 modules: down(silu(gate(x)) * up(x))
         gt = bf16_round(gt);
         ut = bf16_round(ut);
-        hv = bf16_round(gt / (1.f + expf(-gt))) * ut;
+        hb[t] = bf16_round(bf16_round(gt * __frcp_rn(1.f + __expf(-gt))) * ut);
       } else {
-        hv = gt / (1.f + expf(-gt)) * ut;
+        hb[t] = bf16_round(gt * __frcp_rn(1.f + __expf(-gt)) * ut);
       }
-      h[static_cast<size_t>(t) * p.I + kUpHalf * blk + r] = __float2bfloat16_rn(hv);
     }
+    am[t] = fabsf(hb[t]);
   }
   __syncwarp();
   if (lane == 0) mbar_arrive(&aux.upv_empty);  // upv may be rewritten for the next item
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int t = 0; t < kMaxT; ++t)
+      if (t < p.T) am[t] = fmaxf(am[t], __shfl_xor_sync(0xffffffffu, am[t], o));
+  uint8_t* img = p.ws + L.himg + static_cast<size_t>(slot) * L.himg_stride;
+  const int kk = kUpHalf * blk + r;  // k index of the down projection
+  float ex[kMaxT];
+#pragma unroll
+  for (int t = 0; t < kMaxT; t += 2) {
+    if (t >= p.T) {
+      ex[t] = ex[t + 1] = 1.f;
+      continue;
+    }
+    const int e0 = split_exponent(am[t]), e1 = split_exponent(am[t + 1]);
+    ex[t] = exp2i(-e0);
+    ex[t + 1] = exp2i(-e1);
+    uint16_t hi, lo;
+    split2(hb[t] * exp2i(e0), hb[t + 1] * exp2i(e1), hi, lo);
+    if (t < p.T) {
+      img[tc::swz_offset(t, kk, kN)] = static_cast<uint8_t>(hi & 0xFF);
+      img[tc::swz_offset(4 + t, kk, kN)] = static_cast<uint8_t>(lo & 0xFF);
+    }
+    if (t + 1 < p.T) {
+      img[tc::swz_offset(t + 1, kk, kN)] = static_cast<uint8_t>(hi >> 8);
+      img[tc::swz_offset(5 + t, kk, kN)] = static_cast<uint8_t>(lo >> 8);
+    }
+  }
+  if (lane == 0) {
+    float* hinv = reinterpret_cast<float*>(p.ws + L.hinv) + (static_cast<size_t>(slot) * (kMaxI / kGroup) + kk / kGroup) * kMaxT;
+    *reinterpret_cast<float4*>(hinv) = make_float4(ex[0], ex[1], ex[2], ex[3]);
+  }
 }
 
-// Down: thread r holds output row 128*nb + r of one slot; the partial is weighted by the routing
-// weight (the shared slot stays raw: the combine kernel rounds and gates it). Releases the
-// accumulator buffer and the activation tile once both have been read.
+// Down: thread r holds output row 128*nb + r of one slot; accumulator j covers the 32 k of one
+// group of h, weighted by the weight's 128-block scale and the group's 2^-e. The partial carries the
+// routing weight (the shared slot stays raw: the combine kernel rounds and gates it). Releases the
+// accumulator buffer once it has been read.
 __device__ void epilogue_down(const Params& p, const WsLayout& L, Aux& aux, uint32_t taddr, uint64_t* acc_empty,
-                              uint64_t* b_free, const uint32_t* hmax, int slot, int nb, int e, int lane) {
-  const int r = 32 * e + lane, n = kBlockRows * nb + r;
-  const int nkb = p.I / 128;
-  const ExpertRef ex = expert_ref(p, slot, aux.tab.expert);
-  const float* srow = ex.s2 + static_cast<size_t>(n / ex.srows) * nkb;
-  float sc[kMaxI / 128];
-#pragma unroll
-  for (int kb = 0; kb < kMaxI / 128; ++kb) sc[kb] = kb < nkb ? __ldg(srow + kb) : 0.f;
+                              int slot, int nb, int e, int lane, const float (&sc)[kMaxI / 128],
+                              const float4 (&hv)[kMaxI / kGroup]) {
+  const int r = 32 * e + lane;
+  const int ngroups = p.I / kGroup;
   float acc[kMaxT];
-  reduce_kblocks<kMaxI / 128>(taddr, nkb, sc, acc);
+  reduce_acc<kMaxI / kGroup>(
+      taddr, ngroups,
+      [&](int j, int t) {
+        const float4 h = hv[j];
+        return sc[j / (128 / kGroup)] * (t == 0 ? h.x : t == 1 ? h.y : t == 2 ? h.z : h.w);
+      },
+      acc);
   tc::fence_before_sync();
-  float k[kMaxT];
-  const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
-#pragma unroll
-  for (int t = 0; t < kMaxT; ++t)
-    k[t] = exp2i(-split_exponent(__uint_as_float(hmax[t]))) * (shared_slot ? 1.f : aux.tab.coef[slot * kMaxT + t]);
   __syncwarp();
-  if (lane == 0) {
-    mbar_arrive(acc_empty);
-    mbar_arrive(b_free);
-  }
+  if (lane == 0) mbar_arrive(acc_empty);
+  const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
   float* part = partial_block(p, L, nb, slot);
-  for (int t = 0; t < p.T; ++t) __stcg(part + t * kBlockRows + r, acc[t] * k[t]);
+  for (int t = 0; t < p.T; ++t)
+    __stcg(part + t * kBlockRows + r, acc[t] * (shared_slot ? 1.f : aux.tab.coef[slot * kMaxT + t]));
 }
 
 // ------------------------------------------------------------------ up / down kernels
@@ -669,13 +846,15 @@ __device__ void epilogue_down(const Params& p, const WsLayout& L, Aux& aux, uint
 // assigned statically (CTA c takes items c, c + gridDim, ...), so CTAs never wait on each other.
 // map_w covers the routed experts ([E][rows][K] bytes), map_sh the shared expert.
 //
-// Route table: with the router in the layer, epilogue warps 4 .. 4+T-1 select one row's experts
-// each (up: after the wait, since the route kernel is the predecessor; down: before it, since the
-// route kernel has completed by the time the down kernel starts) and warp 4 builds the table; with
-// routing given, warp 4 builds it from the caller's ids.
+// Route table: warp 4 reads the one the route kernel wrote (or builds it from the caller's ids).
+// The up kernel reads it after griddepcontrol.wait; the down kernel before it, since everything it
+// needs from the route kernel (or from the kernel that produced the ids) completed before the up
+// kernel released its dependents. The down kernel's activation tiles come from the up kernel and
+// are copied in after the wait.
 template <bool DOWN>
 __global__ void __launch_bounds__(kThreads, 1)
-    expert_kernel(const Params p, const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_sh) {
+    expert_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map_w,
+                  const __grid_constant__ CUtensorMap map_sh) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const SmemLayout S = smem_layout(DOWN, p.H, p.I);
@@ -701,21 +880,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&aux.acc_empty[a], kEpiThreads / 32);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&aux.b_ready[b], kSplitThreads);
-      mbar_init(&aux.b_free[b], kEpiThreads / 32);
+      mbar_init(&aux.b_ready[b], 1);  // the producer's arrive.expect_tx; the copy completes it
+      mbar_init(&aux.b_free[b], 1);   // tcgen05.commit after the item's MMAs
     }
     mbar_init(&aux.upv_full, 2);   // the two up-row warps
     mbar_init(&aux.upv_empty, 2);  // the two gate-row warps
     fence_mbar_init();
   }
   if (warp == kWarpMma) tc::tmem_alloc(&aux.tmem, tmem_cols);
-  if (DOWN && warp >= kWarpSplit && warp < kWarpEpi) {
-    // the rows of the activation tiles that no item writes stay zero
-    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-    for (int i = tid - kWarpSplit * 32; i < 2 * S.b_bytes / 16; i += kSplitThreads)
-      reinterpret_cast<uint4*>(smem + S.b)[i] = z;
-    tc::fence_proxy_async_smem();
-  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -763,7 +935,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::prefetch_map(&map_w);
       if (sh) tc::prefetch_map(&map_sh);
     }
-    int k = 0, c = 0;  // item ordinal and chunk of the next stage
+    int k = 0, c = 0;  // item ordinal and chunk of the next weight stage
     if (!DOWN && sh) {
       // shared-expert stages need no routing: up to one ring of them before the table exists
       for (int n = 0; ok && n < S.nstages; ++n) {
@@ -776,21 +948,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    named_bar(kBarSelect, kThreads);
     named_bar(kBarTable, kThreads);
     const int n_items = aux.n_slots * per_slot;
-    while (ok) {
-      const int idx = blockIdx.x + k * gridDim.x;
-      if (idx >= n_items) break;
-      ok = issue(idx, c);
-      if (++c == nchunks) {
-        c = 0;
-        ++k;
+    auto item_of = [&](int kk) { return static_cast<int>(blockIdx.x) + kk * static_cast<int>(gridDim.x); };
+    if (!DOWN) {
+      while (ok && item_of(k) < n_items) {
+        ok = issue(item_of(k), c);
+        if (++c == nchunks) {
+          c = 0;
+          ++k;
+        }
+      }
+    } else {
+      // weights of the first ring before the wait; afterwards each item's activation tile (from the
+      // up kernel) is copied in ahead of any further weight stage of a later item
+      for (int n = 0; ok && n < S.nstages && item_of(k) < n_items; ++n) {
+        ok = issue(item_of(k), c);
+        if (++c == nchunks) {
+          c = 0;
+          ++k;
+        }
+      }
+      griddep_wait();
+      griddep_launch();
+      if (lane == 0) fence_proxy_async();
+      int kb = 0;  // next item whose activation tile is copied
+      while (ok) {
+        const bool b_due = item_of(kb) < n_items && kb <= k;
+        if (b_due) {
+          const int bb = kb & 1;
+          bool ready = true;
+          if (lane == 0) ready = mbar_wait(&aux.b_free[bb], ((kb >> 1) & 1) ^ 1u);
+          ready = __shfl_sync(0xffffffffu, ready, 0);
+          if (!ready) {
+            if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+            break;
+          }
+          if (lane == 0) {
+            const int slot = item_of(kb) / per_slot;
+            mbar_arrive_expect_tx(&aux.b_ready[bb], static_cast<uint32_t>(S.b_bytes));
+            bulk_g2s(smem + S.b + bb * S.b_bytes, p.ws + L.himg + static_cast<size_t>(slot) * L.himg_stride,
+                     static_cast<uint32_t>(S.b_bytes), &aux.b_ready[bb]);
+          }
+          __syncwarp();
+          ++kb;
+        } else if (item_of(k) < n_items) {
+          ok = issue(item_of(k), c);
+          if (++c == nchunks) {
+            c = 0;
+            ++k;
+          }
+        } else {
+          break;
+        }
       }
     }
   } else if (warp == kWarpMma) {
     // ================================================================ MMA issuer
-    named_bar(kBarSelect, kThreads);
+    if (!DOWN) {
+      griddep_wait();  // x comes from the preceding kernel
+      griddep_launch();
+      split_x(p, smem + S.b, aux, lane);  // the MMA warp helps split x (split index 0-31)
+    }
     named_bar(kBarTable, kThreads);
     tc::fence_after_sync();
     const int n_items = aux.n_slots * per_slot;
@@ -829,9 +1048,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 2 && 2 * c + j < nkb; ++j) {
             const int kb = 2 * c + j;
 #pragma unroll
-            for (int k4 = 0; k4 < 4; ++k4)
-              tc::mma_f8(d + kb * 16, tc::smem_desc(a + j * kSlabBytes + 32 * k4),
-                         tc::smem_desc(bt + kb * kBSlabBytes + 32 * k4), idesc, k4 > 0);
+            for (int k4 = 0; k4 < 4; ++k4) {
+              // up: one accumulator per 128-wide k block; down: one per 32-wide group of h
+              const uint32_t col = DOWN ? (kb * 4 + k4) * 16 : kb * 16;
+              tc::mma_f8(d + col, tc::smem_desc(a + j * kSlabBytes + 32 * k4),
+                         tc::smem_desc(bt + kb * kBSlabBytes + 32 * k4), idesc, DOWN ? false : k4 > 0);
+            }
           }
           tc::mma_commit(&aux.empty[stage]);  // the stage is free once these MMAs have read it
         }
@@ -841,39 +1063,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           full_par ^= 1u;
         }
       }
-      if (ok && lane == 0) tc::mma_commit(&aux.acc_full[ab]);
+      if (ok && lane == 0) {
+        tc::mma_commit(&aux.acc_full[ab]);
+        if (DOWN) tc::mma_commit(&aux.b_free[bb]);
+      }
       __syncwarp();
     }
   } else if (warp < kWarpEpi) {
-    // ================================================================ activation split
-    const int ptid = tid - kWarpSplit * 32;
+    // ================================================================ warps 2-3: split x (up)
     if (!DOWN) {
       griddep_wait();
       griddep_launch();
-      split_x(p, smem + S.b, aux, ptid);
-      named_bar(kBarSelect, kThreads);
-      named_bar(kBarTable, kThreads);
-    } else {
-      named_bar(kBarSelect, kThreads);
-      named_bar(kBarTable, kThreads);
-      griddep_wait();  // h comes from the up kernel
-      griddep_launch();
-      const int n_items = aux.n_slots * per_slot;
-      for (int k = 0;; ++k) {
-        const int idx = blockIdx.x + k * gridDim.x;
-        if (idx >= n_items) break;
-        const int bb = k & 1;
-        // one thread waits; the outcome reaches both warps through shared memory and a barrier
-        if (ptid == 0) {
-          aux.split_ok = mbar_wait(&aux.b_free[bb], ((k >> 1) & 1) ^ 1u) ? 1 : 0;
-          if (!aux.split_ok) flag_error(p, L, STATUS_TIMEOUT);
-        }
-        named_bar(kBarSplit, kSplitThreads);
-        if (!aux.split_ok) break;
-        split_h(p, L, smem + S.b + bb * S.b_bytes, aux.hmax[bb], idx / per_slot, ptid);
-        mbar_arrive(&aux.b_ready[bb]);
-      }
+      split_x(p, smem + S.b, aux, 32 + (warp - 2) * 32 + lane);
     }
+    named_bar(kBarTable, kThreads);
   } else {
     // ================================================================ epilogue (+ route table)
     const int e = warp - kWarpEpi;  // TMEM lane quarter (warp % 4)
@@ -881,32 +1084,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       griddep_wait();
       griddep_launch();
     }
-    if (p.mode == 1 && e < p.T) route_row(p, L, e, lane, tab, !DOWN && blockIdx.x == 0);
-    named_bar(kBarSelect, kThreads);
     if (warp == kWarpEpi) {
-      const int n = p.mode == 1 ? table_from_selection(p, lane, tab) : table_from_ids(p, L, lane, tab, !DOWN);
+      const int n = p.mode == 1 ? table_from_ws(p, L, lane, tab) : table_from_ids(p, L, lane, tab, !DOWN);
       if (lane == 0) aux.n_slots = n;
+    } else if (!DOWN) {
+      split_x(p, smem + S.b, aux, 96 + (warp - kWarpEpi - 1) * 32 + lane);
     }
     named_bar(kBarTable, kThreads);
     if (DOWN) {
       griddep_wait();
       griddep_launch();
-      if (blockIdx.x == 0 && warp == kWarpEpi) {
-        // the combine kernel reads the slot count and the shared gate of this call from the workspace
-        if (lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(aux.n_slots);
-        if (lane < p.T) reinterpret_cast<float*>(p.ws + L.coef)[lane] = tab.coef[lane];
-      }
+      if (p.mode == 0 && blockIdx.x == 0 && warp == kWarpEpi && lane == 0)
+        ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(aux.n_slots);  // for the combine kernel
     }
     const int n_items = aux.n_slots * per_slot;
     for (int k = 0;; ++k) {
       const int idx = blockIdx.x + k * gridDim.x;
       if (idx >= n_items) break;
-      const int ab = k % nacc, bb = k & 1;
-      bool ready = true;
-      if (lane == 0) {
-        ready = mbar_wait(&aux.acc_full[ab], (k / nacc) & 1);
-        if (ready && DOWN) ready = mbar_wait(&aux.b_ready[bb], (k >> 1) & 1);
+      const int ab = k % nacc;
+      const int slot = idx / per_slot, blk = idx % per_slot;
+      const ExpertRef ex = expert_ref(p, slot, tab.expert);
+      const int r = 32 * e + lane;
+      float sc13[kMaxH / 128], sc2[kMaxI / 128];
+      float4 hv[kMaxI / kGroup];
+      if (!DOWN) {
+        const int wrow = r < kUpHalf ? kUpHalf * blk + r : p.I + kUpHalf * blk + (r - kUpHalf);
+        load_scales(ex.s13 + static_cast<size_t>(wrow / ex.srows) * nkb, nkb, sc13, kMaxH / 128);
+      } else {
+        load_scales(ex.s2 + static_cast<size_t>((kBlockRows * blk + r) / ex.srows) * nkb, nkb, sc2, kMaxI / 128);
+        const float4* hsrc =
+            reinterpret_cast<const float4*>(p.ws + L.hinv) + static_cast<size_t>(slot) * (kMaxI / kGroup);
+#pragma unroll
+        for (int g = 0; g < kMaxI / kGroup; ++g)
+          hv[g] = g < p.I / kGroup ? __ldcg(hsrc + g) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      bool ready = true;
+      if (lane == 0) ready = mbar_wait(&aux.acc_full[ab], (k / nacc) & 1);
       ready = __shfl_sync(0xffffffffu, ready, 0);
       if (!ready) {
         if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
@@ -915,10 +1128,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * e) << 16) + ab * acc_cols;
       if (!DOWN)
-        epilogue_up(p, L, aux, taddr, &aux.acc_empty[ab], idx / per_slot, idx % per_slot, e, lane, k);
+        epilogue_up(p, L, aux, taddr, &aux.acc_empty[ab], slot, blk, e, lane, k, sc13);
       else
-        epilogue_down(p, L, aux, taddr, &aux.acc_empty[ab], &aux.b_free[bb], aux.hmax[bb], idx / per_slot,
-                      idx % per_slot, e, lane);
+        epilogue_down(p, L, aux, taddr, &aux.acc_empty[ab], slot, blk, e, lane, sc2, hv);
     }
   }
 
@@ -932,7 +1144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // y = bf16(bf16(bf16(sum of routed partials) + bias) + bf16(sigmoid gate * bf16(shared))): the
 // rounding points of fp8_moe_forward's bf16 output, Speaker's bias add (engine.py:236-237) and
 // speaker_forward's bf16 tensor sum (engine.py:158). One thread per output element.
-__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const Params p) {
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_constant__ Params p) {
   const WsLayout L = ws_layout(p.H, p.I);
   const int e = blockIdx.x * kCombineThreads + threadIdx.x;
   const int t = e / p.H, n = e % p.H;
@@ -1013,8 +1225,12 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
                                     cudaSharedmemCarveoutMaxShared) == cudaSuccess;
     ok = ok && cudaFuncSetAttribute(moe::expert_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     cudaSharedmemCarveoutMaxShared) == cudaSuccess;
-    ok = ok && cudaFuncSetAttribute(moe::route_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                    cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    for (auto k : {moe::route_kernel<false>, moe::route_kernel<true>}) {
+      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(moe::route_smem_bytes(kMaxH, true))) == cudaSuccess;
+      ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    }
     ok = ok && cudaFuncSetAttribute(moe::combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     cudaSharedmemCarveoutMaxShared) == cudaSuccess;
     if (!ok) {
@@ -1045,8 +1261,10 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
   int launches = 0;
   if (p.mode == 1) {
     const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
-    if (int rc = launch_one(moe::route_kernel, (rows + moe::kRouteWarps - 1) / moe::kRouteWarps,
-                            moe::kRouteWarps * 32, 0, stream, "moe route", p))
+    const bool w32 = p.router_bf16 == 0;
+    if (int rc = launch_one(w32 ? moe::route_kernel<true> : moe::route_kernel<false>,
+                            (rows + moe::kRouteWarps - 1) / moe::kRouteWarps, moe::kRouteWarps * 32,
+                            moe::route_smem_bytes(p.H, w32), stream, "moe route", p))
       return rc;
     ++launches;
   }
@@ -1208,7 +1426,7 @@ extern "C" int dm3_moe_status(void* workspace, uint32_t* status, void* stream) {
 // caller-provided workspace. Every GPU that loads the library reserves it until the process exits.
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 1310720;  // 1.25 MiB: the workspace of H <= 2048, I <= 512
+constexpr size_t kNoAllocScratchBytes = 1572864;  // 1.5 MiB: the workspace of H <= 2048, I <= 512
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 // Device address of g_noalloc_scratch per device; the host-side symbol is not a device address.
 void* g_noalloc_ptr[64] = {nullptr};
@@ -1225,7 +1443,7 @@ extern "C" int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const v
   dm3::note_launches(0);
   if (H > 0 && I > 0 && H <= dm3::kMaxH && I <= dm3::kMaxI &&
       dm3::moe_ws_bytes(H, I) > kNoAllocScratchBytes)
-    return dm3::set_error("H and I need more scratch than the 1.25 MiB static array holds"), 4;
+    return dm3::set_error("H and I need more scratch than the 1.5 MiB static array holds"), 4;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return dm3::set_error("no usable current CUDA device"), 2;

@@ -144,7 +144,7 @@ int dm3_moe_status(void* workspace, uint32_t* status, void* stream);
  * dm3_moe_layer without a workspace argument, for callers that cannot allocate device memory:
  * code running inside another runtime's memory pool, plugin hosts that only hand out their own
  * buffers, or paths where cudaMalloc is not allowed. It has no counterpart in the reference.
- * Arguments and results are those of dm3_moe_layer. The scratch is a 1.25 MiB array compiled
+ * Arguments and results are those of dm3_moe_layer. The scratch is a 1.5 MiB array compiled
  * into the library, held by every GPU that loads it until the process exits; H <= 2048 and
  * I <= 512 always fit, and sizes beyond the array are rejected with DM3_ENOSPACE. The first
  * call on a device looks up the array's address and zeroes it on the given stream, so make
