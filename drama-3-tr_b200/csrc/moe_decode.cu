@@ -55,7 +55,9 @@ constexpr int kBSlabBytes = kN * 128;         // one K slab of the activation ti
 constexpr int kUpStages = 5, kDownStages = 6;
 constexpr int kUpAcc = 2, kDownAcc = 2;       // TMEM accumulator buffers
 constexpr uint32_t kUpTmemCols = 512, kDownTmemCols = 512;
-constexpr int kRouteWarps = 4;      // router rows per route CTA (one warp per row)
+constexpr int kRouteWarps = 4;      // router rows per route CTA
+constexpr int kRouteSplit = 4;      // warps per router row (each sums a quarter of H)
+constexpr int kRouteThreads = kRouteWarps * kRouteSplit * 32;
 constexpr int kCombineThreads = 256;
 // named barriers (0 is __syncthreads)
 constexpr int kBarTable = 1, kBarSplit = 2;
@@ -99,7 +101,7 @@ struct Params {
 // serves every T of a given (H, I). Nothing in it carries state from one call to the next except
 // the sticky status word (the route kernel's CTA counter is back at zero after every call).
 struct WsLayout {
-  size_t ctrl, slot_expert, coef, logits, himg, himg_stride, hinv, partial, total;
+  size_t ctrl, slot_expert, coef, logits, himg, himg_stride, hinv, ximg, xinv, partial, total;
 };
 enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
 
@@ -124,6 +126,12 @@ __host__ __device__ inline WsLayout ws_layout(int H, int I) {
   o += L.himg_stride * kMaxSlots;
   L.hinv = o;  // [kMaxSlots][kMaxI / kGroup][kMaxT] fp32: 2^-e of each 32-element group of h
   o += static_cast<size_t>(kMaxSlots) * (kMaxI / kGroup) * kMaxT * 4;
+  // x split by the route kernel into the up kernel's activation tile (16 rows x H), and 2^-e per row
+  o = align_up(o, 1024);
+  L.ximg = o;
+  o += static_cast<size_t>(H / 128) * kBSlabBytes;
+  L.xinv = o;
+  o += kMaxT * 4;
   o = align_up(o, 128);
   L.partial = o;  // [H / 128][kMaxSlots][kMaxT][128] fp32: one output block's slots are adjacent
   o += static_cast<size_t>(H / kBlockRows) * kMaxSlots * kMaxT * kBlockRows * 4;
@@ -323,9 +331,36 @@ __device__ __forceinline__ void warp_top8(uint64_t (&k)[8]) {
   }
 }
 
+// ------------------------------------------------------------------ activation split
+// 16 consecutive bf16 values, prescaled by sc, split exactly into e4m3 hi and lo bytes.
+__device__ __forceinline__ void split16(const uint4 (&v)[2], float sc, uint4& hi, uint4& lo) {
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(v);
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint16_t h0, l0, h1, l1;
+    split2(__bfloat162float(e[4 * i]) * sc, __bfloat162float(e[4 * i + 1]) * sc, h0, l0);
+    split2(__bfloat162float(e[4 * i + 2]) * sc, __bfloat162float(e[4 * i + 3]) * sc, h1, l1);
+    h[i] = h0 | (static_cast<uint32_t>(h1) << 16);
+    l[i] = l0 | (static_cast<uint32_t>(l1) << 16);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ float abs_max16(const uint4 (&v)[2]) {
+  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(v);
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(__bfloat162float(e[i])));
+  return m;
+}
+
 // Shared-memory tail of the route kernel: the logits of every row (the last column is the shared
 // expert's gate), the selections and the table scratch of the last CTA.
 struct RouteTail {
+  float2 part[kRouteWarps][kMaxT][kRouteSplit];  // (hi, lo) of each warp's quarter of a row
+  uint32_t xmax[kMaxT];
   float logits[kMaxT][kMaxRouter + 1];
   int sel_e[kMaxT * kMaxTopK];
   float sel_w[kMaxT * kMaxTopK];
@@ -496,25 +531,27 @@ __host__ __device__ inline size_t route_smem_bytes(int H, bool w32) {
   return route_tail_offset(H, w32) + align_up(sizeof(RouteTail), 16);
 }
 
-// Router logits, then the route table. One warp per router row (plus the shared expert's gate
-// row). The CTA's rows are copied into shared memory by the bulk-copy engine before
-// griddepcontrol.wait (router weights never depend on the preceding kernel); the activation rows
-// are staged after it. Every product is exact in fp32 (bf16 x bf16; bf16 x fp32 keeps its rounding
-// error through an fma) and is summed as a hi + lo pair, which carries about 48 significant bits,
-// so the logit is the sum rounded once to fp32 (then to bf16 for a bf16 router), + the optional
-// logit bias. The shared gate row is rounded to bf16 as a bf16 linear's output. The last CTA to
-// finish (one gpu-scope fence per CTA, with no copies in flight) selects the experts of every row
-// (one warp per row) and writes the table.
+// Router logits, then the route table. Four warps per router row (plus the shared expert's gate
+// row), each summing a quarter of H. The CTA's rows are copied into shared memory by the bulk-copy
+// engine before griddepcontrol.wait (router weights never depend on the preceding kernel); the
+// activation rows are staged after it. Every product is exact in fp32 (bf16 x bf16; bf16 x fp32
+// keeps its rounding error through an fma) and is summed as a hi + lo pair, which carries about 48
+// significant bits, so the logit is the sum rounded once to fp32 (then to bf16 for a bf16 router),
+// + the optional logit bias. The shared gate row is rounded to bf16 as a bf16 linear's output.
+// Each CTA also splits its share of x into the up kernel's activation tile (the exact e4m3 hi / lo
+// of x * 2^e per row). The last CTA to finish (one gpu-scope fence per CTA, with no copies in
+// flight) selects the experts of every row (one warp per row) and writes the table.
 template <bool W32>
-__global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(16) uint8_t rsm[];
   const WsLayout L = ws_layout(p.H, p.I);
   const int H = p.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rw = warp / kRouteSplit, quarter = warp % kRouteSplit;  // row within the CTA, quarter of H
   const bool sh_gate_row = p.sh_w13 != nullptr && p.sh_gate != nullptr;
   const int rows = p.n_router + (sh_gate_row ? 1 : 0);
   const int row0 = blockIdx.x * kRouteWarps;
-  const int row = row0 + warp;
+  const int row = row0 + rw;
   const int wsz = W32 ? 4 : 2;
   uint8_t* wrows = rsm;  // [kRouteWarps][H] weights
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm + static_cast<size_t>(kRouteWarps) * H * wsz);
@@ -533,22 +570,61 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_co
         bulk_g2s(wrows + static_cast<size_t>(r - row0) * H * wsz, p.sh_gate, H * 2, &rt.bar);
     }
   }
+  if (threadIdx.x < kMaxT) rt.xmax[threadIdx.x] = 0u;
+  __syncthreads();  // the maxima are zero before any thread folds into them
   griddep_wait();
   griddep_launch();
-  const uint4* xsrc = reinterpret_cast<const uint4*>(p.x);
-  for (int c = threadIdx.x; c < p.T * H / 8; c += kRouteWarps * 32) reinterpret_cast<uint4*>(xs)[c] = xsrc[c];
+  {
+    constexpr int kPer = kMaxT * kMaxH / 8 / kRouteThreads;
+    const int n16 = p.T * H / 8;
+    const uint4* xsrc = reinterpret_cast<const uint4*>(p.x);
+    uint4 v[kPer];
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int c = threadIdx.x + q * kRouteThreads;
+      v[q] = c < n16 ? xsrc[c] : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int q = 0; q < kPer; ++q) {
+      const int c = threadIdx.x + q * kRouteThreads;
+      if (c < n16) {
+        reinterpret_cast<uint4*>(xs)[c] = v[q];
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[q]);
+        float m = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(__bfloat162float(e[i])));
+        atomicMax(&rt.xmax[c / (H / 8)], __float_as_uint(m));
+      }
+    }
+  }
   if (threadIdx.x == 0 && !mbar_wait(&rt.bar, 0)) flag_error(p, L, STATUS_TIMEOUT);
   __syncthreads();
+  // this CTA's share of the x split: 16-element chunks c = blockIdx.x + gridDim.x * j
+  {
+    uint8_t* img = p.ws + L.ximg;
+    const int chunks = H / 16;
+    for (int c = blockIdx.x + gridDim.x * static_cast<int>(threadIdx.x); c < p.T * chunks;
+         c += gridDim.x * kRouteThreads) {
+      const int t = c / chunks, k = (c % chunks) * 16;
+      const uint4 v2[2] = {*reinterpret_cast<const uint4*>(xs + t * H + k), *reinterpret_cast<const uint4*>(xs + t * H + k + 8)};
+      uint4 hi, lo;
+      split16(v2, exp2i(split_exponent(__uint_as_float(rt.xmax[t]))), hi, lo);
+      *reinterpret_cast<uint4*>(img + tc::swz_offset(t, k, kN)) = hi;
+      *reinterpret_cast<uint4*>(img + tc::swz_offset(4 + t, k, kN)) = lo;
+    }
+    if (blockIdx.x == 0 && threadIdx.x < kMaxT)
+      reinterpret_cast<float*>(p.ws + L.xinv)[threadIdx.x] = exp2i(-split_exponent(__uint_as_float(rt.xmax[threadIdx.x])));
+  }
   float* logits = reinterpret_cast<float*>(p.ws + L.logits);
   if (row < rows) {
-    const bool is_router = row < p.n_router;
-    const bool row_w32 = W32 && is_router;  // the shared gate row is bf16 in either case
-    const uint8_t* wr = wrows + static_cast<size_t>(warp) * H * wsz;
+    const bool row_w32 = W32 && row < p.n_router;  // the shared gate row is bf16 in either case
+    const uint8_t* wr = wrows + static_cast<size_t>(rw) * H * wsz;
+    const int k0 = quarter * (H / kRouteSplit), k1 = k0 + H / kRouteSplit;
     for (int t = 0; t < p.T; ++t) {
       const __nv_bfloat16* xr = xs + t * H;
       float hi[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, lo[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-      for (int k = lane * 8; k < H; k += 256) {
+      for (int k = k0 + lane * 8; k < k1; k += 256) {
         const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
         const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
         float w[8];
@@ -582,16 +658,27 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_co
         l += __shfl_xor_sync(0xffffffffu, l, o);
         two_sum_acc(h, l, oh);
       }
-      if (lane == 0) {
-        float v = h + l;
-        if (is_router) {
-          if (p.logits_bf16) v = bf16_round(v);
-          if (p.logit_bias) v += p.logit_bias[row];
-        } else {
-          v = bf16_round(v);
-        }
-        logits[t * (kMaxRouter + 1) + row] = v;
+      if (lane == 0) rt.part[rw][t][quarter] = make_float2(h, l);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < kRouteWarps * kMaxT) {
+    const int r = threadIdx.x / kMaxT, t = threadIdx.x % kMaxT;
+    if (row0 + r < rows && t < p.T) {
+      float h = rt.part[r][t][0].x, l = rt.part[r][t][0].y;
+#pragma unroll
+      for (int q = 1; q < kRouteSplit; ++q) {
+        l += rt.part[r][t][q].y;
+        two_sum_acc(h, l, rt.part[r][t][q].x);
       }
+      float v = h + l;
+      if (row0 + r < p.n_router) {
+        if (p.logits_bf16) v = bf16_round(v);
+        if (p.logit_bias) v += p.logit_bias[row0 + r];
+      } else {
+        v = bf16_round(v);
+      }
+      logits[t * (kMaxRouter + 1) + row0 + r] = v;
     }
   }
   __syncthreads();
@@ -605,16 +692,16 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_co
   if (!rt.last) return;
   // last CTA: every logit is visible
   {
-    constexpr int kPer = (kMaxT * (kMaxRouter + 1) + kRouteWarps * 32 - 1) / (kRouteWarps * 32);
+    constexpr int kPer = (kMaxT * (kMaxRouter + 1) + kRouteThreads - 1) / kRouteThreads;
     float v[kPer];
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int i = threadIdx.x + q * kRouteWarps * 32;
+      const int i = threadIdx.x + q * kRouteThreads;
       v[q] = i < p.T * (kMaxRouter + 1) && i % (kMaxRouter + 1) < rows ? __ldcg(logits + i) : 0.f;
     }
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int i = threadIdx.x + q * kRouteWarps * 32;
+      const int i = threadIdx.x + q * kRouteThreads;
       if (i < kMaxT * (kMaxRouter + 1)) (&rt.logits[0][0])[i] = v[q];
     }
   }
@@ -625,31 +712,6 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_kernel(const __grid_co
     write_table(p, L, rt, lane);
     if (lane == 0) ctrl(p, L)[CTRL_ROUTE_COUNT] = 0u;  // every CTA has counted: ready for the next call
   }
-}
-
-// ------------------------------------------------------------------ activation split
-// 16 consecutive bf16 values, prescaled by sc, split exactly into e4m3 hi and lo bytes.
-__device__ __forceinline__ void split16(const uint4 (&v)[2], float sc, uint4& hi, uint4& lo) {
-  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(v);
-  uint32_t h[4], l[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint16_t h0, l0, h1, l1;
-    split2(__bfloat162float(e[4 * i]) * sc, __bfloat162float(e[4 * i + 1]) * sc, h0, l0);
-    split2(__bfloat162float(e[4 * i + 2]) * sc, __bfloat162float(e[4 * i + 3]) * sc, h1, l1);
-    h[i] = h0 | (static_cast<uint32_t>(h1) << 16);
-    l[i] = l0 | (static_cast<uint32_t>(l1) << 16);
-  }
-  hi = make_uint4(h[0], h[1], h[2], h[3]);
-  lo = make_uint4(l[0], l[1], l[2], l[3]);
-}
-
-__device__ __forceinline__ float abs_max16(const uint4 (&v)[2]) {
-  const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(v);
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(__bfloat162float(e[i])));
-  return m;
 }
 
 // Up: the activation tile of all H. Row t holds the e4m3 hi part of x[t] * 2^e_t (e_t maps the
@@ -948,6 +1010,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (!DOWN && p.mode == 1) {
+      // the route kernel left x split into this kernel's activation tile: one bulk copy from L2
+      griddep_wait();
+      griddep_launch();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&aux.b_ready[0], static_cast<uint32_t>(S.b_bytes));
+        bulk_g2s(smem + S.b, p.ws + L.ximg, static_cast<uint32_t>(S.b_bytes), &aux.b_ready[0]);
+      }
+      __syncwarp();
+    }
     named_bar(kBarTable, kThreads);
     const int n_items = aux.n_slots * per_slot;
     auto item_of = [&](int kk) { return static_cast<int>(blockIdx.x) + kk * static_cast<int>(gridDim.x); };
@@ -1005,12 +1077,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     // ================================================================ MMA issuer
-    if (!DOWN) {
+    if (!DOWN && p.mode == 0) {
       griddep_wait();  // x comes from the preceding kernel
       griddep_launch();
       split_x(p, smem + S.b, aux, lane);  // the MMA warp helps split x (split index 0-31)
     }
     named_bar(kBarTable, kThreads);
+    if (!DOWN && p.mode == 1) {
+      bool got = true;
+      if (lane == 0) got = mbar_wait(&aux.b_ready[0], 0);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got && lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+    }
     tc::fence_after_sync();
     const int n_items = aux.n_slots * per_slot;
     const uint32_t idesc = tc::idesc_e4m3(kTileRows, kN);
@@ -1070,8 +1148,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
   } else if (warp < kWarpEpi) {
-    // ================================================================ warps 2-3: split x (up)
-    if (!DOWN) {
+    // ================================================================ warps 2-3: split x (up, routing given)
+    if (!DOWN && p.mode == 0) {
       griddep_wait();
       griddep_launch();
       split_x(p, smem + S.b, aux, 32 + (warp - 2) * 32 + lane);
@@ -1087,7 +1165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kWarpEpi) {
       const int n = p.mode == 1 ? table_from_ws(p, L, lane, tab) : table_from_ids(p, L, lane, tab, !DOWN);
       if (lane == 0) aux.n_slots = n;
-    } else if (!DOWN) {
+      if (!DOWN && p.mode == 1 && lane < kMaxT) aux.xinv[lane] = __ldcg(reinterpret_cast<const float*>(p.ws + L.xinv) + lane);
+    } else if (!DOWN && p.mode == 0) {
       split_x(p, smem + S.b, aux, 96 + (warp - kWarpEpi - 1) * 32 + lane);
     }
     named_bar(kBarTable, kThreads);
@@ -1263,7 +1342,7 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
     const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
     const bool w32 = p.router_bf16 == 0;
     if (int rc = launch_one(w32 ? moe::route_kernel<true> : moe::route_kernel<false>,
-                            (rows + moe::kRouteWarps - 1) / moe::kRouteWarps, moe::kRouteWarps * 32,
+                            (rows + moe::kRouteWarps - 1) / moe::kRouteWarps, moe::kRouteThreads,
                             moe::route_smem_bytes(p.H, w32), stream, "moe route", p))
       return rc;
     ++launches;
