@@ -60,7 +60,7 @@ constexpr int kRouteSplit = 4;      // warps per router row (each sums a quarter
 constexpr int kRouteThreads = kRouteWarps * kRouteSplit * 32;
 constexpr int kCombineThreads = 256;
 // named barriers (0 is __syncthreads)
-constexpr int kBarTable = 1, kBarSplit = 2;
+constexpr int kBarTable = 1, kBarSplit = 2, kBarEpi = 3;
 
 struct Params {
   int T, H, I, top_k;
@@ -157,8 +157,8 @@ struct Aux {
   uint64_t full[8], empty[8];        // TMA ring: bytes landed / MMAs done reading
   uint64_t acc_full[4], acc_empty[4];  // TMEM accumulators: MMAs done / epilogue done reading
   uint64_t b_ready[2], b_free[2];    // activation tiles (down): copied in / MMAs done reading
-  uint64_t upv_full, upv_empty;      // up: up-row values written / read
   uint32_t tmem;
+  int epi_ok[4];                     // up: each epilogue warp's accumulator wait succeeded
   int n_slots;
   float xinv[kMaxT];                 // up: 2^-e of each token's split
   uint32_t xmax[kMaxT];              // up: |x| maxima (float bits)
@@ -789,10 +789,11 @@ __device__ __forceinline__ void load_scales(const float* srow, int nkb, float* s
 // through shared memory to the gate threads, which apply SwiGLU, round h to bf16 (the reference's
 // activation dtype) and write it straight into the down kernel's activation tile: each warp's 32
 // values of a token form one group whose power-of-two scale maps its absolute maximum into
-// [128, 256), and h * 2^e splits exactly into e4m3 hi + lo. Releases the accumulator buffer
+// [128, 256), and h * 2^e splits exactly into e4m3 hi + lo. The four epilogue warps meet at a
+// named barrier (the caller makes their loop decisions uniform). Releases the accumulator buffer
 // (acc_empty) as soon as it has been read.
 __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32_t taddr, uint64_t* acc_empty,
-                            int slot, int blk, int e, int lane, int k, const float (&sc)[kMaxH / 128]) {
+                            int slot, int blk, int e, int lane, const float (&sc)[kMaxH / 128]) {
   const int r = 32 * e + lane;
   const int nkb = p.H / 128;
   float acc[kMaxT];
@@ -800,28 +801,14 @@ __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32
   tc::fence_before_sync();
   __syncwarp();
   if (lane == 0) mbar_arrive(acc_empty);
-  // hand-off of the up values through shared memory, guarded by two mbarriers (bounded waits)
-  const uint32_t par = static_cast<uint32_t>(k & 1);
-  if (r >= kUpHalf) {
-    bool ok = true;
-    if (lane == 0) ok = mbar_wait(&aux.upv_empty, par ^ 1u);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    if (!ok && lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+  if (r >= kUpHalf)
 #pragma unroll
     for (int t = 0; t < kMaxT; ++t) aux.upv[r - kUpHalf][t] = acc[t] * aux.xinv[t];
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&aux.upv_full);
-    return;
-  }
-  bool ok = true;
-  if (lane == 0) ok = mbar_wait(&aux.upv_full, par);
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  if (!ok) {
-    if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
-    return;
-  }
+  named_bar(kBarEpi, kEpiThreads);
+  if (r >= kUpHalf) return;
   const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
-  float hb[kMaxT], am[kMaxT];
+  float hb[kMaxT];
+  uint32_t am[kMaxT];
 #pragma unroll
   for (int t = 0; t < kMaxT; ++t) {
     hb[t] = 0.f;
@@ -839,15 +826,8 @@ __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32
         hb[t] = bf16_round(gt * __frcp_rn(1.f + __expf(-gt)) * ut);
       }
     }
-    am[t] = fabsf(hb[t]);
+    am[t] = t < p.T ? __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(hb[t]))) : 0u;
   }
-  __syncwarp();
-  if (lane == 0) mbar_arrive(&aux.upv_empty);  // upv may be rewritten for the next item
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int t = 0; t < kMaxT; ++t)
-      if (t < p.T) am[t] = fmaxf(am[t], __shfl_xor_sync(0xffffffffu, am[t], o));
   uint8_t* img = p.ws + L.himg + static_cast<size_t>(slot) * L.himg_stride;
   const int kk = kUpHalf * blk + r;  // k index of the down projection
   float ex[kMaxT];
@@ -857,15 +837,13 @@ __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32
       ex[t] = ex[t + 1] = 1.f;
       continue;
     }
-    const int e0 = split_exponent(am[t]), e1 = split_exponent(am[t + 1]);
+    const int e0 = split_exponent(__uint_as_float(am[t])), e1 = split_exponent(__uint_as_float(am[t + 1]));
     ex[t] = exp2i(-e0);
     ex[t + 1] = exp2i(-e1);
     uint16_t hi, lo;
     split2(hb[t] * exp2i(e0), hb[t + 1] * exp2i(e1), hi, lo);
-    if (t < p.T) {
-      img[tc::swz_offset(t, kk, kN)] = static_cast<uint8_t>(hi & 0xFF);
-      img[tc::swz_offset(4 + t, kk, kN)] = static_cast<uint8_t>(lo & 0xFF);
-    }
+    img[tc::swz_offset(t, kk, kN)] = static_cast<uint8_t>(hi & 0xFF);
+    img[tc::swz_offset(4 + t, kk, kN)] = static_cast<uint8_t>(lo & 0xFF);
     if (t + 1 < p.T) {
       img[tc::swz_offset(t + 1, kk, kN)] = static_cast<uint8_t>(hi >> 8);
       img[tc::swz_offset(5 + t, kk, kN)] = static_cast<uint8_t>(lo >> 8);
@@ -945,8 +923,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&aux.b_ready[b], 1);  // the producer's arrive.expect_tx; the copy completes it
       mbar_init(&aux.b_free[b], 1);   // tcgen05.commit after the item's MMAs
     }
-    mbar_init(&aux.upv_full, 2);   // the two up-row warps
-    mbar_init(&aux.upv_empty, 2);  // the two gate-row warps
     fence_mbar_init();
   }
   if (warp == kWarpMma) tc::tmem_alloc(&aux.tmem, tmem_cols);
@@ -1200,6 +1176,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ready = true;
       if (lane == 0) ready = mbar_wait(&aux.acc_full[ab], (k / nacc) & 1);
       ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!DOWN) {
+        // the up epilogue's warps meet at named barriers: they continue or stop together
+        if (lane == 0) aux.epi_ok[e] = ready ? 1 : 0;
+        named_bar(kBarEpi, kEpiThreads);
+        ready = aux.epi_ok[0] && aux.epi_ok[1] && aux.epi_ok[2] && aux.epi_ok[3];
+        named_bar(kBarEpi, kEpiThreads);  // epi_ok may be rewritten for the next item
+      }
       if (!ready) {
         if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
         break;
@@ -1207,7 +1190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * e) << 16) + ab * acc_cols;
       if (!DOWN)
-        epilogue_up(p, L, aux, taddr, &aux.acc_empty[ab], slot, blk, e, lane, k, sc13);
+        epilogue_up(p, L, aux, taddr, &aux.acc_empty[ab], slot, blk, e, lane, sc13);
       else
         epilogue_down(p, L, aux, taddr, &aux.acc_empty[ab], slot, blk, e, lane, sc2, hv);
     }
