@@ -231,7 +231,8 @@ def run_decode(args, world, rank, local, speaker=False):
         torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    launches = args.steps * n_layers
+    # kernels per layer as the library reports them (route, up, down, combine)
+    launches = args.steps * n_layers * dm3._lib.load().dm3_last_launch_count()
 
     # end to end through the public op with host buffers: every layer's rows H2D from pinned memory
     # (one copy), the captured frame, and the frame's result (the last layer's rows) D2H
@@ -294,9 +295,9 @@ def run_decode(args, world, rank, local, speaker=False):
             "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4),
             "peak_source": f"{pk['source']} HBM copy bandwidth",
-            "kernel": "dm3::moe::moe_decode_kernel",
+            "kernel": "one decode layer: dm3::moe route + up + down + combine kernels",
             "bytes_per_launch": round(bytes_step / n_layers),
-            "traffic": recorded_traffic("moe_decode_kernel"),
+            "traffic": recorded_traffic("moe_decode_layer"),
         },
         "gpu_launches": launches,
         "e2e": {

@@ -911,6 +911,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_cols = DOWN ? kDownTmemCols : kUpTmemCols;
 
   if (tid == 0) {
+    // the TMA descriptors are fetched while the CTA sets up
+    tc::prefetch_map(&map_w);
+    if (sh) tc::prefetch_map(&map_sh);
     for (int s = 0; s < S.nstages; ++s) {
       mbar_init(&aux.full[s], 1);   // the producer's arrive.expect_tx; the TMA bytes complete it
       mbar_init(&aux.empty[s], 1);  // tcgen05.commit after the stage's MMAs
@@ -932,172 +935,140 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = aux.tmem;
 
   if (warp == kWarpTma) {
-    // ================================================================ TMA producer
+    // ================================================================ TMA producer (lane 0 issues)
     int stage = 0;
     uint32_t empty_par = 1;
     bool ok = true;
     auto issue = [&](int idx, int c) -> bool {
-      bool ready = true;
-      if (lane == 0) ready = mbar_wait(&aux.empty[stage], empty_par);
-      ready = __shfl_sync(0xffffffffu, ready, 0);
-      if (!ready) {
-        if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
+      if (!mbar_wait(&aux.empty[stage], empty_par)) {
+        flag_error(p, L, STATUS_TIMEOUT);
         return false;
       }
-      if (lane == 0) {
-        const int slot = idx / per_slot, blk = idx % per_slot;
-        const bool shared_slot = sh && slot == 0;
-        const CUtensorMap* map = shared_slot ? &map_sh : &map_w;
-        const int ex = shared_slot ? 0 : tab.expert[slot];
-        uint8_t* dst = smem + S.stage + stage * kStageBytes;
-        const int kb0 = 2 * c, nsl = min(2, nkb - kb0);
-        mbar_arrive_expect_tx(&aux.full[stage], static_cast<uint32_t>(nsl * kSlabBytes));
-        for (int j = 0; j < nsl; ++j) {
-          const int kx = (kb0 + j) * 128;
-          if (!DOWN) {
-            tc::tma_load_3d(dst + j * kSlabBytes, map, kx, kUpHalf * blk, ex, &aux.full[stage]);
-            tc::tma_load_3d(dst + j * kSlabBytes + kSlabBytes / 2, map, kx, p.I + kUpHalf * blk, ex, &aux.full[stage]);
-          } else {
-            tc::tma_load_3d(dst + j * kSlabBytes, map, kx, kBlockRows * blk, ex, &aux.full[stage]);
-          }
+      const int slot = idx / per_slot, blk = idx % per_slot;
+      const bool shared_slot = sh && slot == 0;
+      const CUtensorMap* map = shared_slot ? &map_sh : &map_w;
+      const int ex = shared_slot ? 0 : tab.expert[slot];
+      uint8_t* dst = smem + S.stage + stage * kStageBytes;
+      const int kb0 = 2 * c, nsl = min(2, nkb - kb0);
+      mbar_arrive_expect_tx(&aux.full[stage], static_cast<uint32_t>(nsl * kSlabBytes));
+      for (int j = 0; j < nsl; ++j) {
+        const int kx = (kb0 + j) * 128;
+        if (!DOWN) {
+          tc::tma_load_3d(dst + j * kSlabBytes, map, kx, kUpHalf * blk, ex, &aux.full[stage]);
+          tc::tma_load_3d(dst + j * kSlabBytes + kSlabBytes / 2, map, kx, p.I + kUpHalf * blk, ex, &aux.full[stage]);
+        } else {
+          tc::tma_load_3d(dst + j * kSlabBytes, map, kx, kBlockRows * blk, ex, &aux.full[stage]);
         }
       }
-      __syncwarp();
       if (++stage == S.nstages) {
         stage = 0;
         empty_par ^= 1u;
       }
       return true;
     };
-    if (lane == 0) {
-      tc::prefetch_map(&map_w);
-      if (sh) tc::prefetch_map(&map_sh);
-    }
     int k = 0, c = 0;  // item ordinal and chunk of the next weight stage
-    if (!DOWN && sh) {
-      // shared-expert stages need no routing: up to one ring of them before the table exists
-      for (int n = 0; ok && n < S.nstages; ++n) {
-        const int idx = blockIdx.x + k * gridDim.x;
-        if (idx >= per_slot) break;
-        ok = issue(idx, c);
-        if (++c == nchunks) {
-          c = 0;
-          ++k;
+    auto item_of = [&](int kk) { return static_cast<int>(blockIdx.x) + kk * static_cast<int>(gridDim.x); };
+    auto advance = [&]() {
+      if (++c == nchunks) {
+        c = 0;
+        ++k;
+      }
+    };
+    if (lane == 0) {
+      if (!DOWN && sh) {
+        // shared-expert stages need no routing: up to one ring of them before the table exists
+        for (int n = 0; ok && n < S.nstages && item_of(k) < per_slot; ++n) {
+          ok = issue(item_of(k), c);
+          advance();
         }
       }
-    }
-    if (!DOWN && p.mode == 1) {
-      // the route kernel left x split into this kernel's activation tile: one bulk copy from L2
-      griddep_wait();
-      griddep_launch();
-      if (lane == 0) {
+      if (!DOWN && p.mode == 1) {
+        // the route kernel left x split into this kernel's activation tile: one bulk copy from L2
+        griddep_wait();
+        griddep_launch();
         mbar_arrive_expect_tx(&aux.b_ready[0], static_cast<uint32_t>(S.b_bytes));
         bulk_g2s(smem + S.b, p.ws + L.ximg, static_cast<uint32_t>(S.b_bytes), &aux.b_ready[0]);
       }
-      __syncwarp();
     }
+    __syncwarp();
     named_bar(kBarTable, kThreads);
     const int n_items = aux.n_slots * per_slot;
-    auto item_of = [&](int kk) { return static_cast<int>(blockIdx.x) + kk * static_cast<int>(gridDim.x); };
-    if (!DOWN) {
-      while (ok && item_of(k) < n_items) {
-        ok = issue(item_of(k), c);
-        if (++c == nchunks) {
-          c = 0;
-          ++k;
+    if (lane == 0) {
+      if (!DOWN) {
+        while (ok && item_of(k) < n_items) {
+          ok = issue(item_of(k), c);
+          advance();
         }
-      }
-    } else {
-      // weights of the first ring before the wait; afterwards each item's activation tile (from the
-      // up kernel) is copied in ahead of any further weight stage of a later item
-      for (int n = 0; ok && n < S.nstages && item_of(k) < n_items; ++n) {
-        ok = issue(item_of(k), c);
-        if (++c == nchunks) {
-          c = 0;
-          ++k;
+      } else {
+        // weights of the first ring before the wait; afterwards each item's activation tile (from
+        // the up kernel) is copied in ahead of any further weight stage of a later item
+        for (int n = 0; ok && n < S.nstages && item_of(k) < n_items; ++n) {
+          ok = issue(item_of(k), c);
+          advance();
         }
-      }
-      griddep_wait();
-      griddep_launch();
-      if (lane == 0) fence_proxy_async();
-      int kb = 0;  // next item whose activation tile is copied
-      while (ok) {
-        const bool b_due = item_of(kb) < n_items && kb <= k;
-        if (b_due) {
-          const int bb = kb & 1;
-          bool ready = true;
-          if (lane == 0) ready = mbar_wait(&aux.b_free[bb], ((kb >> 1) & 1) ^ 1u);
-          ready = __shfl_sync(0xffffffffu, ready, 0);
-          if (!ready) {
-            if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
-            break;
-          }
-          if (lane == 0) {
+        griddep_wait();
+        griddep_launch();
+        fence_proxy_async();
+        int kb = 0;  // next item whose activation tile is copied
+        while (ok) {
+          if (item_of(kb) < n_items && kb <= k) {
+            const int bb = kb & 1;
+            if (!mbar_wait(&aux.b_free[bb], ((kb >> 1) & 1) ^ 1u)) {
+              flag_error(p, L, STATUS_TIMEOUT);
+              break;
+            }
             const int slot = item_of(kb) / per_slot;
             mbar_arrive_expect_tx(&aux.b_ready[bb], static_cast<uint32_t>(S.b_bytes));
             bulk_g2s(smem + S.b + bb * S.b_bytes, p.ws + L.himg + static_cast<size_t>(slot) * L.himg_stride,
                      static_cast<uint32_t>(S.b_bytes), &aux.b_ready[bb]);
+            ++kb;
+          } else if (item_of(k) < n_items) {
+            ok = issue(item_of(k), c);
+            advance();
+          } else {
+            break;
           }
-          __syncwarp();
-          ++kb;
-        } else if (item_of(k) < n_items) {
-          ok = issue(item_of(k), c);
-          if (++c == nchunks) {
-            c = 0;
-            ++k;
-          }
-        } else {
-          break;
         }
       }
     }
+    __syncwarp();
   } else if (warp == kWarpMma) {
-    // ================================================================ MMA issuer
+    // ================================================================ MMA issuer (lane 0 issues)
     if (!DOWN && p.mode == 0) {
       griddep_wait();  // x comes from the preceding kernel
       griddep_launch();
       split_x(p, smem + S.b, aux, lane);  // the MMA warp helps split x (split index 0-31)
     }
     named_bar(kBarTable, kThreads);
-    if (!DOWN && p.mode == 1) {
-      bool got = true;
-      if (lane == 0) got = mbar_wait(&aux.b_ready[0], 0);
-      got = __shfl_sync(0xffffffffu, got, 0);
-      if (!got && lane == 0) flag_error(p, L, STATUS_TIMEOUT);
-    }
-    tc::fence_after_sync();
     const int n_items = aux.n_slots * per_slot;
-    const uint32_t idesc = tc::idesc_e4m3(kTileRows, kN);
-    int stage = 0;
-    uint32_t full_par = 0;
-    bool ok = true;
-    for (int k = 0; ok; ++k) {
-      const int idx = blockIdx.x + k * gridDim.x;
-      if (idx >= n_items) break;
-      const int ab = k % nacc, bb = k & 1;
-      bool ready = true;
-      if (lane == 0) {
-        ready = mbar_wait(&aux.acc_empty[ab], ((k / nacc) & 1) ^ 1u);
-        if (ready && DOWN) ready = mbar_wait(&aux.b_ready[bb], (k >> 1) & 1);
+    if (lane == 0) {
+      bool ok = true;
+      if (!DOWN && p.mode == 1 && !mbar_wait(&aux.b_ready[0], 0)) {
+        flag_error(p, L, STATUS_TIMEOUT);
+        ok = false;
       }
-      ready = __shfl_sync(0xffffffffu, ready, 0);
-      if (!ready) {
-        if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
-        break;
-      }
-      tc::fence_after_sync();
-      const uint32_t bt = smem_u32(smem + S.b + (DOWN ? bb * S.b_bytes : 0));
-      const uint32_t d = tmem + ab * acc_cols;
-      for (int c = 0; c < nchunks; ++c) {
-        if (lane == 0) ready = mbar_wait(&aux.full[stage], full_par);
-        ready = __shfl_sync(0xffffffffu, ready, 0);
-        if (!ready) {
-          if (lane == 0) flag_error(p, L, STATUS_TIMEOUT);
-          ok = false;
+      const uint32_t idesc = tc::idesc_e4m3(kTileRows, kN);
+      int stage = 0;
+      uint32_t full_par = 0;
+      for (int k = 0; ok; ++k) {
+        const int idx = blockIdx.x + k * gridDim.x;
+        if (idx >= n_items) break;
+        const int ab = k % nacc, bb = k & 1;
+        if (!mbar_wait(&aux.acc_empty[ab], ((k / nacc) & 1) ^ 1u) ||
+            (DOWN && !mbar_wait(&aux.b_ready[bb], (k >> 1) & 1))) {
+          flag_error(p, L, STATUS_TIMEOUT);
           break;
         }
-        tc::fence_after_sync();
-        if (lane == 0) {
+        tc::fence_after_sync();  // the epilogue's reads of this accumulator are ordered before the MMAs
+        const uint32_t bt = smem_u32(smem + S.b + (DOWN ? bb * S.b_bytes : 0));
+        const uint32_t d = tmem + ab * acc_cols;
+        for (int c = 0; c < nchunks; ++c) {
+          // the TMA's bytes completing the stage's barrier make them visible to the tensor core
+          if (!mbar_wait(&aux.full[stage], full_par)) {
+            flag_error(p, L, STATUS_TIMEOUT);
+            ok = false;
+            break;
+          }
           const uint32_t a = smem_u32(smem + S.stage + stage * kStageBytes);
           for (int j = 0; j < 2 && 2 * c + j < nkb; ++j) {
             const int kb = 2 * c + j;
@@ -1110,19 +1081,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           tc::mma_commit(&aux.empty[stage]);  // the stage is free once these MMAs have read it
+          if (++stage == S.nstages) {
+            stage = 0;
+            full_par ^= 1u;
+          }
         }
-        __syncwarp();
-        if (++stage == S.nstages) {
-          stage = 0;
-          full_par ^= 1u;
-        }
-      }
-      if (ok && lane == 0) {
+        if (!ok) break;
         tc::mma_commit(&aux.acc_full[ab]);
         if (DOWN) tc::mma_commit(&aux.b_free[bb]);
       }
-      __syncwarp();
     }
+    __syncwarp();
   } else if (warp < kWarpEpi) {
     // ================================================================ warps 2-3: split x (up, routing given)
     if (!DOWN && p.mode == 0) {
