@@ -262,6 +262,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
 }  // namespace gemv
 
 // ------------------------------------------------------------------ host launcher
+int launch_gemv_tc(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q, int64_t ldq, const float* s,
+                   int64_t lds, int srows, const void* bias, int bias_kind, void* y, int64_t ldy, int y_fp32,
+                   cudaStream_t stream);
+
 int launch_gemv(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q, int64_t ldq, const int64_t* rows,
                 int64_t n_rows_q, const float* s, int64_t lds, int srows, const void* bias, int bias_kind, void* y,
                 int64_t ldy, int y_fp32, cudaStream_t stream) {
@@ -350,6 +354,11 @@ extern "C" int dm3_fp8_gemv(const void* x, int M, int K, int N, const void* q, i
   dm3::note_launches(0);
   const int rc = check_gemv(x, M, K, N, q, ldq, s, lds, srows, bias_kind, bias, y, ldy);
   if (rc) return rc;
+  // contiguous weight rows: the tensor-core kernel (split-K over a thread-block cluster)
+  const int rt = dm3::launch_gemv_tc(static_cast<const __nv_bfloat16*>(x), M, K, N, static_cast<const uint8_t*>(q),
+                                     ldq, s, lds, srows, bias, bias_kind, y, ldy, y_fp32,
+                                     static_cast<cudaStream_t>(stream));
+  if (rt >= 0) return rt;
   return dm3::launch_gemv(static_cast<const __nv_bfloat16*>(x), M, K, N, static_cast<const uint8_t*>(q), ldq,
                           nullptr, N, s, lds, srows, bias, bias_kind, y, ldy, y_fp32,
                           static_cast<cudaStream_t>(stream));
