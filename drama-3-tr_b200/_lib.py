@@ -34,6 +34,13 @@ SIGNATURES = {
     "dm3_moe_status": (_i, [_p, _u32p, _p]),
     "dm3_moe_layer_noalloc": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i,
                                    _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p]),
+    "dm3_moe_prefill_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "dm3_moe_prefill": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p,
+                             _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "dm3_moe_grouped": (_i, [_p, _i, _i, _i, _p, _p, _i, _i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p, _p,
+                             _p, _sz, _p]),
+    "dm3_route_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "dm3_route": (_i, [_p, _i, _i, _p, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
     "dm3_last_launch_count": (_i, []),
 }
 

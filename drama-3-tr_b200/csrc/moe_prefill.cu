@@ -1,0 +1,1202 @@
+// Prefill (prompt-reading) MoE layer for B200 (sm_100a): hundreds of tokens against 256 block-FP8
+// experts, as seven chained kernels under programmatic dependent launch.
+//
+//   logits    approximate router logits x . W^T on the tensor cores (tcgen05 kind::f16, bf16 x bf16
+//             products, fp32 accumulation in TMEM), plus the squared norms of the router rows
+//   select    one warp per token: a proven error window around every approximate logit picks the
+//             few experts that can still reach the top k; only those are recomputed exactly (fp64
+//             sums of the exact bf16 products, rounded once), so the chosen experts and their
+//             weights are those of exact logits; softmax / top-k / renormalise as Speaker.__call__
+//             (engine.py:233-235) and the shared expert's sigmoid gate (engine.py:158)
+//   plan      one CTA: the (token, k) pairs stably sorted by expert (the dispatch order), per-expert
+//             offsets, and tiles of up to 64 tokens of one expert (the shared expert takes all T)
+//   dispatch  every (expert, token) position gets the token's row split exactly into e4m3 hi + lo
+//             rows (x * 2^e, one power of two per token), in the permuted order
+//   up        items (tile, 128 gate rows + the matching 128 up rows): tcgen05 kind::f8f6f4 with
+//             M = 128 weight rows, N = 2 x tokens (hi / lo rows interleaved), one fp32 accumulator
+//             pair per 128-wide k slab that the epilogue scales by the weight's block scale into
+//             registers; SwiGLU; h rounded to bf16 and split exactly into e4m3 hi + lo per (token,
+//             128-block of h)
+//   down      items (tile, 128 output rows) against h, per-slab scales (weight block x h block);
+//             one fp32 row per (expert, token) position
+//   combine   per token the routing-weighted sum of its k rows (fixed order), + bias, + the gated
+//             shared expert, with the reference's bf16 rounding points
+//
+// Warp roles of the up / down kernels (one CTA per SM, 10 warps): warp 0 issues TMA loads (weight
+// slabs of 128 rows x 128 bytes and the tile's activation slab), warp 1 issues the MMAs, warps 2-9
+// read the accumulators (warp % 4 selects the TMEM lane quarter, (warp - 2) / 4 the half of the
+// tile's tokens). Every wait is bounded; a wait that runs out sets the status word and the CTA's
+// abort flag, after which no thread waits again and every loop still runs to its end, so no
+// barrier is left without its arrivals.
+#include <cfloat>
+#include <cmath>
+#include <string>
+#include <utility>
+
+#include "dm3_common.cuh"
+#include "dm3_internal.h"
+#include "dm3_route.cuh"
+#include "dm3_tc.cuh"
+
+namespace dm3 {
+namespace pf {
+
+constexpr int kTileTok = 64;                 // tokens per expert tile
+constexpr int kRows = 128;                   // weight rows per MMA tile (M)
+constexpr int kSlab = kRows * 128;           // one 128-byte K slab of a 128-row tile
+constexpr int kThreads = 320;                // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kUpStages = 4, kDownStages = 6;
+constexpr int kUpStage = 3 * kSlab;          // gate slab, up slab, activation slab (<= 128 rows)
+constexpr int kDownStage = 2 * kSlab;        // weight slab, activation slab
+constexpr int kUpAcc = 2, kDownAcc = 4;      // TMEM accumulator buffers (256 / 128 columns each)
+constexpr int kLgK = 512;                    // K per logits CTA
+constexpr int kLgSlabs = kLgK / 64;          // 64 bf16 per 128-byte slab
+constexpr int kLgTok = 32;                   // tokens per logits CTA (N)
+constexpr int kLgThreads = 192;              // warp 0 TMA + MMA, warp 1 TMEM, warps 2-5 epilogue
+constexpr int kLgBSlab = kLgTok * 128;
+constexpr int kLgSmem = kLgSlabs * (kSlab + kLgBSlab) + 1024 + 256;
+constexpr int kSelWarps = 8;
+constexpr int kPlanThreads = 1024;
+constexpr int kDispatchWarps = 8;
+constexpr int kCombineThreads = 256;
+constexpr int kBarEpi = 1;                   // named barrier of the up epilogue's warps
+
+// control words; the status word sits where the decode workspace keeps it, so one reader serves both
+enum : int { C_STATUS = 4, C_NTILES = 8, C_NVALID = 9, C_WORDS = 16 };
+
+struct Params {
+  int T, H, I, E, K;  // tokens, hidden, intermediate, routed experts (router width), top-k
+  int mode;           // 0: routing given (ids / rw), 1: router
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* router_w;  // [E][H] bf16
+  int logits_bf16;
+  const float* logit_bias;
+  const __nv_bfloat16* sh_gate;  // [H] or null
+  const int64_t* ids;
+  const __nv_bfloat16* rw;
+  const uint8_t* w13;
+  int64_t w13_stride;
+  const float* s13;
+  int64_t s13_stride;
+  const uint8_t* w2;
+  int64_t w2_stride;
+  const float* s2;
+  int64_t s2_stride;
+  int srows;
+  const uint8_t* sh_w13;
+  const float* sh_s13;
+  const uint8_t* sh_w2;
+  const float* sh_s2;
+  int sh_srows;
+  const float* out_bias;
+  __nv_bfloat16* y;
+  int64_t* ids_out;
+  __nv_bfloat16* w_out;
+  int64_t* perm_out;
+  int64_t* offsets_out;
+  uint8_t* ws;
+};
+
+// ------------------------------------------------------------------ workspace layout
+// Positions: the P = T * K routed (token, k) pairs in dispatch order (expert-major, stable), then
+// one position per token for the shared expert. Every per-position buffer is indexed by position.
+struct Layout {
+  size_t ctrl, lpart, wnorm, pair_e, pair_w, gate, xexp, pos_tok, perm, inv, tiles, pimg, himg, hinv, outp, total;
+  int ks, max_tiles, npos;
+};
+
+__host__ __device__ inline size_t aup(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+__host__ __device__ inline Layout layout(int T, int H, int I, int E, int K) {
+  Layout L;
+  const size_t P = static_cast<size_t>(T) * K;
+  L.ks = (H + kLgK - 1) / kLgK;
+  L.npos = static_cast<int>(P) + T;
+  L.max_tiles = static_cast<int>((P + kTileTok - 1) / kTileTok) + (E < static_cast<int>(P) ? E : static_cast<int>(P)) +
+                (T + kTileTok - 1) / kTileTok + 1;
+  size_t o = 0;
+  L.ctrl = o;
+  o += C_WORDS * 4;
+  L.lpart = o = aup(o, 128);
+  o += static_cast<size_t>(L.ks) * T * E * 4;
+  L.wnorm = o = aup(o, 128);
+  o += static_cast<size_t>(L.ks) * E * 4;
+  L.pair_e = o = aup(o, 128);
+  o += P * 4;
+  L.pair_w = o = aup(o, 128);
+  o += P * 4;
+  L.gate = o = aup(o, 128);
+  o += static_cast<size_t>(T) * 4;
+  L.xexp = o = aup(o, 128);
+  o += static_cast<size_t>(T) * 4;
+  L.pos_tok = o = aup(o, 128);
+  o += static_cast<size_t>(L.npos) * 4;
+  L.perm = o = aup(o, 128);
+  o += P * 4;
+  L.inv = o = aup(o, 128);
+  o += P * 4;
+  L.tiles = o = aup(o, 128);
+  o += static_cast<size_t>(L.max_tiles) * 16;
+  L.pimg = o = aup(o, 1024);  // [npos][2][H] e4m3: hi row, lo row
+  o += static_cast<size_t>(L.npos) * 2 * H;
+  L.himg = o = aup(o, 1024);  // [npos][2][I] e4m3
+  o += static_cast<size_t>(L.npos) * 2 * I;
+  L.hinv = o = aup(o, 128);   // [npos][I / 128] fp32: 2^-e of each 128-block of h
+  o += static_cast<size_t>(L.npos) * (I / 128) * 4;
+  L.outp = o = aup(o, 128);   // [npos][H] fp32: down-projection row of each position (unweighted)
+  o += static_cast<size_t>(L.npos) * H * 4;
+  L.total = aup(o, 256);
+  return L;
+}
+
+template <typename T>
+__device__ __forceinline__ T* ws_at(const Params& p, size_t off) {
+  return reinterpret_cast<T*>(p.ws + off);
+}
+__device__ __forceinline__ void flag(const Params& p, uint32_t bits) {
+  atomicOr(reinterpret_cast<uint32_t*>(p.ws) + C_STATUS, bits);
+}
+
+// Waits unless the CTA has aborted; a wait that runs out aborts the CTA (and reports it once).
+__device__ __forceinline__ bool wait_or_abort(const Params& p, uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (*abort) return false;
+  if (mbar_wait(bar, parity)) return true;
+  if (!*abort) flag(p, STATUS_TIMEOUT);
+  *abort = 1;
+  return false;
+}
+
+// ------------------------------------------------------------------ logits kernel
+// CTA (m, n, ks): router rows [128 m, +128) x tokens [32 n, +32) over k in [512 ks, +512). Both
+// operands arrive by TMA (the router rows before griddepcontrol.wait, x after it); one thread
+// issues 32 MMAs (M = 128, N = 32, K = 16) into 32 TMEM columns. The partial logits are written
+// as lpart[ks][t][e]; CTAs with n = 0 also write the squared norms of their router rows over their
+// k range, which bound the summation error of the approximate logits.
+__global__ void __launch_bounds__(kLgThreads, 1)
+    logits_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map_r,
+                  const __grid_constant__ CUtensorMap map_x) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + kLgSlabs * kSlab;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + kLgSlabs * kLgBSlab);
+  uint64_t* done = full + kLgSlabs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kRows, t0 = blockIdx.y * kLgTok, ks = blockIdx.z;
+  const int nsl = min(kLgSlabs, p.H / 64 - ks * kLgSlabs);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kLgSlabs; ++s) mbar_init(&full[s], 1);
+    mbar_init(done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 32);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  if (warp == 0) {
+    if (lane == 0) {
+      tc::prefetch_map(&map_r);
+      tc::prefetch_map(&map_x);
+      for (int s = 0; s < nsl; ++s) {
+        mbar_arrive_expect_tx(&full[s], kSlab + kLgBSlab);
+        tc::tma_load_3d(sa + s * kSlab, &map_r, (ks * kLgK + s * 64) * 2, m0, 0, &full[s]);
+      }
+      griddep_wait();  // x comes from the preceding kernel
+      griddep_launch();
+      for (int s = 0; s < nsl; ++s) tc::tma_load_3d(sb + s * kLgBSlab, &map_x, (ks * kLgK + s * 64) * 2, t0, 0, &full[s]);
+      const uint32_t idesc = tc::idesc_bf16(kRows, kLgTok);
+      bool ok = true;
+      for (int s = 0; s < nsl && ok; ++s) {
+        if (!mbar_wait(&full[s], 0)) {
+          flag(p, STATUS_TIMEOUT);
+          ok = false;
+          break;
+        }
+        const uint32_t a = smem_u32(sa + s * kSlab), b = smem_u32(sb + s * kLgBSlab);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc::mma_bf16(tmem, tc::smem_desc(a + 32 * k), tc::smem_desc(b + 32 * k), idesc, s > 0 || k > 0);
+      }
+      tc::mma_commit(done);  // also issued after a failed wait: every MMA issued so far completes
+    }
+    __syncwarp();
+  } else if (warp >= 2) {
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    if (blockIdx.y == 0) {
+      // squared norm of router row m0 + r over this k range (the slab swizzle only permutes
+      // 16-byte chunks inside the row's 128 bytes)
+      float n2 = 0.f;
+      for (int s = 0; s < nsl; ++s) {
+        if (!mbar_wait(&full[s], 0)) {
+          flag(p, STATUS_TIMEOUT);
+          break;
+        }
+        const uint4* row = reinterpret_cast<const uint4*>(sa + s * kSlab + (r >> 3) * 1024 + (r & 7) * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = row[c];
+          const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float f = __bfloat162float(e[i]);
+            n2 = fmaf(f, f, n2);
+          }
+        }
+      }
+      if (m0 + r < p.E) ws_at<float>(p, L.wnorm)[ks * p.E + m0 + r] = n2;
+    }
+    const bool ready = mbar_wait(done, 0);
+    if (!ready && lane == 0) flag(p, STATUS_TIMEOUT);
+    tc::fence_after_sync();
+    float v[32];
+    tc::tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16), v);
+    tc::tmem_wait_ld();
+    if (ready && m0 + r < p.E) {
+      float* out = ws_at<float>(p, L.lpart) + (static_cast<size_t>(ks) * p.T + t0) * p.E + m0 + r;
+#pragma unroll
+      for (int j = 0; j < kLgTok; ++j)
+        if (t0 + j < p.T) out[static_cast<size_t>(j) * p.E] = v[j];
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 1) tc::tmem_dealloc(tmem, 32);
+}
+
+// ------------------------------------------------------------------ select kernel
+constexpr int kXC = kMaxH / 256;  // 8-element chunks of a token row per lane
+
+// The router logit of expert e as the reference's oracle defines it: the exact sum of the bf16
+// products (fp64 accumulation of exact fp64 products; 2048 terms keep it within 2^-42 of exact),
+// rounded once to fp32. The whole warp returns the same value.
+__device__ __forceinline__ float exact_dot(const uint4 (&xv)[kXC], const __nv_bfloat16* wrow, int H, int lane) {
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+  for (int i = 0; i < kXC; ++i) {
+    const int k = 256 * i + 8 * lane;
+    if (k < H) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + k));
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&w);
+      const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        acc[j & 3] = fma(static_cast<double>(__bfloat162float(xe[j])), static_cast<double>(__bfloat162float(we[j])), acc[j & 3]);
+    }
+  }
+  double s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return __double2float_rn(s);
+}
+
+// The logit the softmax sees: fp32 (or rounded to bf16 for a bf16 router) + the optional bias.
+// Non-decreasing in v, so bounds on v give bounds on it.
+__device__ __forceinline__ float logit_map(const Params& p, float v, int e) {
+  if (p.logits_bf16) v = bf16_round(v);
+  if (p.logit_bias) v += __ldg(p.logit_bias + e);
+  return v;
+}
+
+// One warp per token. Routing given (mode 0): validates the ids and records the pairs. Router
+// (mode 1): approximate logit a_e = sum of the logits kernel's partials; its error is below
+// d_e = 2^-10 |x| |w_e| (the fp32 tensor-core sums err by far less than 2^-16 of sum |x_k w_ek|,
+// which Cauchy-Schwarz bounds by |x| |w_e|). theta = the k-th largest of map(a_e - d_e); an expert
+// with map(a_e + d_e) < theta has k experts strictly above it and cannot be selected, every other
+// one is a candidate whose logit is recomputed exactly. Selection, softmax and renormalisation then
+// follow the decode router (ties to the lower index), with the exact values of every candidate;
+// the softmax denominator takes the approximate values of the others, whose share cancels in the
+// renormalised weights.
+__global__ void __launch_bounds__(kSelWarps * 32) select_kernel(const __grid_constant__ Params p) {
+  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * kSelWarps + warp;
+  griddep_wait();
+  griddep_launch();
+  if (t >= p.T) return;
+  const int H = p.H, E = p.E, K = p.K;
+  uint4 xv[kXC];
+  float xn2 = 0.f, xm = 0.f;
+#pragma unroll
+  for (int i = 0; i < kXC; ++i) {
+    const int k = 256 * i + 8 * lane;
+    xv[i] = k < H ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * H + k)) : make_uint4(0u, 0u, 0u, 0u);
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[i]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = __bfloat162float(xe[j]);
+      xn2 = fmaf(f, f, xn2);
+      xm = fmaxf(xm, fabsf(f));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    xn2 += __shfl_xor_sync(0xffffffffu, xn2, o);
+    xm = fmaxf(xm, __shfl_xor_sync(0xffffffffu, xm, o));
+  }
+  if (lane == 0) ws_at<int>(p, L.xexp)[t] = split_exponent(xm);
+  int* pair_e = ws_at<int>(p, L.pair_e) + t * K;
+  float* pair_w = ws_at<float>(p, L.pair_w) + t * K;
+  if (p.mode == 0) {
+    if (lane < K) {
+      const int64_t id = p.ids[t * K + lane];
+      const bool ok = id >= 0 && id < E;
+      if (!ok) flag(p, STATUS_BAD_EXPERT);
+      pair_e[lane] = ok ? static_cast<int>(id) : -1;
+      pair_w[lane] = __bfloat162float(p.rw[t * K + lane]);
+    }
+    if (lane == 0) ws_at<float>(p, L.gate)[t] = 1.f;
+    return;
+  }
+  // approximate logits and their windows
+  float fx[8], fu[8];
+  uint64_t dk[8];
+  const float* lp = ws_at<const float>(p, L.lpart);
+  const float* wn = ws_at<const float>(p, L.wnorm);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane + 32 * i;
+    fx[i] = fu[i] = -FLT_MAX;
+    dk[i] = 0ull;
+    if (e < E) {
+      float a = 0.f, w2 = 0.f;
+      for (int s = 0; s < L.ks; ++s) {
+        a += __ldcg(lp + (static_cast<size_t>(s) * p.T + t) * E + e);
+        w2 += __ldcg(wn + s * E + e);
+      }
+      const float d = __fmul_ru(ldexpf(sqrtf(xn2 * w2), -10), 1.001f) + 1e-30f;
+      fx[i] = logit_map(p, a, e);
+      fu[i] = logit_map(p, __fadd_ru(a, d), e);
+      dk[i] = (static_cast<uint64_t>(order_key(logit_map(p, __fsub_rd(a, d), e))) << 32) | static_cast<uint32_t>(~e);
+    }
+  }
+  warp_top8(dk);
+  uint64_t kth = dk[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j)
+    if (j == K - 1) kth = dk[j];
+  const float theta = key_value(static_cast<uint32_t>(kth >> 32));
+  // exact logits of the candidates
+  bool cand[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    cand[i] = lane + 32 * i < E && fu[i] >= theta;
+    unsigned m = __ballot_sync(0xffffffffu, cand[i]);
+    while (m) {
+      const int b = __ffs(m) - 1;
+      m &= m - 1u;
+      const int e = b + 32 * i;
+      const float v = exact_dot(xv, p.router_w + static_cast<size_t>(e) * H, H, lane);
+      if (lane == b) fx[i] = logit_map(p, v, e);
+    }
+  }
+  float gcoef = 1.f;
+  if (p.sh_gate) gcoef = bf16_round(1.f / (1.f + expf(-bf16_round(exact_dot(xv, p.sh_gate, H, lane)))));
+  uint64_t k[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    k[i] = cand[i] ? (static_cast<uint64_t>(order_key(fx[i])) << 32) | static_cast<uint32_t>(~(lane + 32 * i)) : 0ull;
+  warp_top8(k);
+  int sel_e[8];
+  float sel_v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    sel_e[j] = static_cast<int>(~static_cast<uint32_t>(k[j]));
+    sel_v[j] = key_value(static_cast<uint32_t>(k[j] >> 32));
+  }
+  const float m = sel_v[0];
+  float z = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (lane + 32 * i < E) z += expf(fx[i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  int my_e = 0;
+  float my_v = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    if (lane == j) {
+      my_e = sel_e[j];
+      my_v = sel_v[j];
+    }
+  const float my_p = expf(my_v - m) / z;
+  float psum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    const float pj = __shfl_sync(0xffffffffu, my_p, j);
+    if (j < K) psum += pj;
+  }
+  if (lane < K) {
+    const __nv_bfloat16 wb = __float2bfloat16_rn(my_p / psum);
+    pair_e[lane] = my_e;
+    pair_w[lane] = __bfloat162float(wb);
+    if (p.ids_out) p.ids_out[t * K + lane] = my_e;
+    if (p.w_out) p.w_out[t * K + lane] = wb;
+  }
+  if (lane == 0) ws_at<float>(p, L.gate)[t] = gcoef;
+}
+
+// ------------------------------------------------------------------ plan kernel
+// One CTA. Warp w owns pairs [w * per, (w + 1) * per) in pair order; pass 1 counts each expert per
+// warp, a scan over warps and experts gives each (warp, expert) its first position, and pass 2
+// hands out positions in pair order, so the order is the stable sort of the pairs by expert
+// (argsort(ids.flatten(), stable=True)). Tiles: ceil(n_e / 64) per expert, in expert order, then the
+// shared expert's tiles over all T tokens.
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constant__ Params p) {
+  extern __shared__ int psm[];
+  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const int E = p.E, K = p.K, T = p.T, P = T * K;
+  const bool sh = p.sh_w13 != nullptr;
+  int* wc = psm;            // [32][E]
+  int* cnt = wc + 32 * E;   // [E]
+  int* off = cnt + E;       // [E + 1]
+  int* tb = off + E + 1;    // [E + 1]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < 32 * E; i += kPlanThreads) wc[i] = 0;
+  griddep_wait();
+  griddep_launch();
+  __syncthreads();
+  const int* pair_e = ws_at<const int>(p, L.pair_e);
+  const int per = (P + 32 * 32 - 1) / (32 * 32) * 32;
+  for (int r = 0; r < per; r += 32) {
+    const int idx = warp * per + r + lane;
+    const int e = idx < P ? __ldcg(pair_e + idx) : -1;
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(m) - 1) wc[warp * E + e] += __popc(m);
+  }
+  __syncthreads();
+  for (int e = tid; e < E; e += kPlanThreads) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wc[w * E + e];
+      wc[w * E + e] = run;
+      run += c;
+    }
+    cnt[e] = run;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int per_l = (E + 31) / 32;
+    int s = 0, st = 0;
+    for (int j = 0; j < per_l; ++j) {
+      const int e = lane * per_l + j;
+      if (e < E) {
+        s += cnt[e];
+        st += (cnt[e] + kTileTok - 1) / kTileTok;
+      }
+    }
+    int incl = s, inclt = st;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int a = __shfl_up_sync(0xffffffffu, incl, o), b = __shfl_up_sync(0xffffffffu, inclt, o);
+      if (lane >= o) {
+        incl += a;
+        inclt += b;
+      }
+    }
+    int base = incl - s, tbase = inclt - st;
+    for (int j = 0; j < per_l; ++j) {
+      const int e = lane * per_l + j;
+      if (e < E) {
+        off[e] = base;
+        tb[e] = tbase;
+        base += cnt[e];
+        tbase += (cnt[e] + kTileTok - 1) / kTileTok;
+      }
+    }
+    if (lane == 31) {
+      off[E] = incl;
+      tb[E] = inclt;
+    }
+  }
+  __syncthreads();
+  const int nvalid = off[E], nt_routed = tb[E];
+  const int nt_sh = sh ? (T + kTileTok - 1) / kTileTok : 0;
+  int4* tiles = ws_at<int4>(p, L.tiles);
+  for (int e = tid; e < E; e += kPlanThreads) {
+    const int n = cnt[e];
+    for (int j = 0; j * kTileTok < n; ++j) tiles[tb[e] + j] = make_int4(e, off[e] + j * kTileTok, min(kTileTok, n - j * kTileTok), 0);
+  }
+  for (int j = tid; j < nt_sh; j += kPlanThreads) tiles[nt_routed + j] = make_int4(-1, P + j * kTileTok, min(kTileTok, T - j * kTileTok), 0);
+  int* perm = ws_at<int>(p, L.perm);
+  int* pos_tok = ws_at<int>(p, L.pos_tok);
+  int* inv = ws_at<int>(p, L.inv);
+  for (int r = 0; r < per; r += 32) {
+    const int idx = warp * per + r + lane;
+    const int e = idx < P ? __ldcg(pair_e + idx) : -1;
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    const int rank = e >= 0 ? wc[warp * E + e] + __popc(m & ((1u << lane) - 1u)) : 0;
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(m) - 1) wc[warp * E + e] += __popc(m);
+    __syncwarp();
+    if (e >= 0) {
+      const int pos = off[e] + rank;
+      perm[pos] = idx;
+      pos_tok[pos] = idx / K;
+      inv[idx] = pos;
+      if (p.perm_out) p.perm_out[pos] = idx;
+    } else if (idx < P) {
+      inv[idx] = -1;
+    }
+  }
+  for (int t = tid; t < T; t += kPlanThreads) pos_tok[P + t] = t;
+  if (p.offsets_out)
+    for (int e = tid; e <= E; e += kPlanThreads) p.offsets_out[e] = off[e];
+  if (tid == 0) {
+    uint32_t* c = ws_at<uint32_t>(p, L.ctrl);
+    c[C_NTILES] = static_cast<uint32_t>(nt_routed + nt_sh);
+    c[C_NVALID] = static_cast<uint32_t>(nvalid);
+  }
+}
+
+// ------------------------------------------------------------------ dispatch kernel
+// One warp per position: the token's row x * 2^e (e from the token's absolute maximum) split
+// exactly into e4m3 hi and lo rows of the permuted activation image.
+__global__ void __launch_bounds__(kDispatchWarps * 32) dispatch_kernel(const __grid_constant__ Params p) {
+  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = blockIdx.x * kDispatchWarps + warp;
+  const int P = p.T * p.K;
+  griddep_wait();
+  griddep_launch();
+  const int nvalid = static_cast<int>(__ldcg(ws_at<const uint32_t>(p, L.ctrl) + C_NVALID));
+  if (!(pos < nvalid || (p.sh_w13 != nullptr && pos >= P && pos < P + p.T))) return;
+  const int t = __ldcg(ws_at<const int>(p, L.pos_tok) + pos);
+  const float sc = exp2i(__ldcg(ws_at<const int>(p, L.xexp) + t));
+  const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
+  uint8_t* hi_row = p.ws + L.pimg + static_cast<size_t>(2 * pos) * p.H;
+  uint8_t* lo_row = hi_row + p.H;
+  for (int c = lane; c < p.H / 16; c += 32) {
+    const uint4 v[2] = {__ldg(src + 2 * c), __ldg(src + 2 * c + 1)};
+    uint4 hi, lo;
+    split16(v, sc, hi, lo);
+    *reinterpret_cast<uint4*>(hi_row + 16 * c) = hi;
+    *reinterpret_cast<uint4*>(lo_row + 16 * c) = lo;
+  }
+}
+
+// ------------------------------------------------------------------ up / down kernels
+struct Aux {
+  uint64_t full[8], empty[8];
+  uint64_t acc_full[4], acc_empty[4];
+  uint64_t mma_done;
+  uint32_t tmem;
+  int abort;
+  float amax[2][2][4][32];  // up: [item parity][token half][lane quarter][token] |h| maxima
+};
+
+// Activation box of a tile of n tokens: 2n rows rounded up to 16, 32, 64 or 128 (the MMA's N).
+__device__ __forceinline__ int box_index(int n) { return n <= 8 ? 0 : n <= 16 ? 1 : n <= 32 ? 2 : 3; }
+
+template <bool DOWN>
+__global__ void __launch_bounds__(kThreads, 1)
+    expert_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map_w,
+                  const __grid_constant__ CUtensorMap map_sh, const __grid_constant__ CUtensorMap map_b0,
+                  const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_b2,
+                  const __grid_constant__ CUtensorMap map_b3) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr int kStages = DOWN ? kDownStages : kUpStages;
+  constexpr int kStage = DOWN ? kDownStage : kUpStage;
+  constexpr int kBOff = DOWN ? kSlab : 2 * kSlab;  // activation slab inside a stage
+  constexpr int kNacc = DOWN ? kDownAcc : kUpAcc;
+  constexpr uint32_t kAccCols = DOWN ? 128 : 256;
+  Aux& aux = *reinterpret_cast<Aux*>(smem + kStages * kStage);
+  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nrb = (DOWN ? p.H : p.I) / kRows;  // weight row blocks per tile
+  const int nkb = (DOWN ? p.I : p.H) / 128;    // k slabs per item
+  // the plan kernel ran at least two launches back, so its tiles are complete
+  const int ntiles = static_cast<int>(__ldcg(ws_at<const uint32_t>(p, L.ctrl) + C_NTILES));
+  const int n_items = ntiles * nrb;
+  const int my_items = n_items > static_cast<int>(blockIdx.x) ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int4* tiles = ws_at<const int4>(p, L.tiles);
+  volatile int* abort = &aux.abort;
+
+  if (tid == 0) {
+    tc::prefetch_map(&map_w);
+    if (p.sh_w13) tc::prefetch_map(&map_sh);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&aux.full[s], 1);
+      mbar_init(&aux.empty[s], 1);
+    }
+    for (int a = 0; a < kNacc; ++a) {
+      mbar_init(&aux.acc_full[a], 1);
+      mbar_init(&aux.acc_empty[a], kEpiWarps);
+    }
+    mbar_init(&aux.mma_done, 1);
+    aux.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(&aux.tmem, 512);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = aux.tmem;
+
+  if (warp == 0) {
+    // ================================================================ TMA producer (lane 0)
+    if (lane == 0) {
+      const int total = my_items * nkb;
+      auto stage_ptr = [&](int s) { return smem + (s % kStages) * kStage; };
+      auto item_tile = [&](int s, int& rb, int& kb) {
+        const int k = s / nkb;
+        kb = s % nkb;
+        const int idx = blockIdx.x + k * gridDim.x;
+        rb = idx % nrb;
+        return __ldcg(tiles + idx / nrb);
+      };
+      auto issue_a = [&](int s) {
+        int rb, kb;
+        const int4 tl = item_tile(s, rb, kb);
+        const CUtensorMap* map = tl.x < 0 ? &map_sh : &map_w;
+        const int plane = tl.x < 0 ? 0 : tl.x;
+        uint8_t* dst = stage_ptr(s);
+        uint64_t* bar = &aux.full[s % kStages];
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kBOff + (16 << box_index(tl.z)) * 128));
+        tc::tma_load_3d(dst, map, kb * 128, kRows * rb, plane, bar);
+        if (!DOWN) tc::tma_load_3d(dst + kSlab, map, kb * 128, p.I + kRows * rb, plane, bar);
+      };
+      auto issue_b = [&](int s) {
+        int rb, kb;
+        const int4 tl = item_tile(s, rb, kb);
+        const int bi = box_index(tl.z);
+        const CUtensorMap* map = bi == 0 ? &map_b0 : bi == 1 ? &map_b1 : bi == 2 ? &map_b2 : &map_b3;
+        tc::tma_load_3d(stage_ptr(s) + kBOff, map, kb * 128, 2 * tl.y, 0, &aux.full[s % kStages]);
+      };
+      // the weight slabs of the first ring before the wait; activation slabs (from the preceding
+      // kernel) after it
+      const int first = min(total, kStages);
+      for (int s = 0; s < first; ++s) issue_a(s);
+      griddep_wait();
+      griddep_launch();
+      for (int s = 0; s < first; ++s) issue_b(s);
+      for (int s = first; s < total; ++s) {
+        const int st = s % kStages;
+        wait_or_abort(p, &aux.empty[st], ((s / kStages) & 1) ^ 1u, abort);
+        issue_a(s);
+        issue_b(s);
+      }
+      // nothing may still be copying into shared memory when the CTA exits (bounded waits, also
+      // after an abort)
+      for (int s = max(0, total - kStages); s < total; ++s) mbar_wait(&aux.full[s % kStages], (s / kStages) & 1);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer (lane 0)
+    if (lane == 0) {
+      int s = 0, use = 0;
+      for (int k = 0; k < my_items; ++k) {
+        const int idx = blockIdx.x + k * gridDim.x;
+        const int4 tl = __ldcg(tiles + idx / nrb);
+        const uint32_t idesc = tc::idesc_e4m3(kRows, 16 << box_index(tl.z));
+        for (int kb = 0; kb < nkb; ++kb, ++s, ++use) {
+          const int ab = use % kNacc;
+          wait_or_abort(p, &aux.acc_empty[ab], ((use / kNacc) & 1) ^ 1u, abort);
+          wait_or_abort(p, &aux.full[s % kStages], (s / kStages) & 1, abort);
+          tc::fence_after_sync();
+          const uint32_t a = smem_u32(smem + (s % kStages) * kStage);
+          const uint32_t b = a + kBOff;
+          const uint32_t d = tmem + ab * kAccCols;
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            tc::mma_f8(d, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+            if (!DOWN) tc::mma_f8(d + 128, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+          }
+          tc::mma_commit(&aux.empty[s % kStages]);
+          tc::mma_commit(&aux.acc_full[ab]);
+        }
+      }
+      tc::mma_commit(&aux.mma_done);
+      wait_or_abort(p, &aux.mma_done, 0, abort);
+    }
+    __syncwarp();
+  } else {
+    // ================================================================ epilogue (warps 2-9)
+    const int q = warp & 3, hf = (warp - 2) >> 2;
+    const int r = 32 * q + lane;
+    if (DOWN) griddep_wait();  // the h blocks' scales come from the up kernel
+    int use = 0;
+    for (int k = 0; k < my_items; ++k) {
+      const int idx = blockIdx.x + k * gridDim.x;
+      const int4 tl = __ldcg(tiles + idx / nrb);
+      const int rb = idx % nrb;
+      const int nh = min(max(tl.z - 32 * hf, 0), 32);  // this warp's tokens of the tile
+      const int pbase = tl.y + 32 * hf;
+      const bool shared_tile = tl.x < 0;
+      const int srows = shared_tile ? p.sh_srows : p.srows;
+      float a0[32], a1[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a0[j] = a1[j] = 0.f;
+      if (!DOWN) {
+        const float* s13 = shared_tile ? p.sh_s13 : p.s13 + static_cast<size_t>(tl.x) * p.s13_stride;
+        float sg[kMaxH / 128], su[kMaxH / 128];
+        const int rg = kRows * rb + r, ru = p.I + kRows * rb + r;
+#pragma unroll
+        for (int kb = 0; kb < kMaxH / 128; ++kb) {
+          sg[kb] = kb < nkb ? __ldg(s13 + static_cast<size_t>(rg / srows) * nkb + kb) : 0.f;
+          su[kb] = kb < nkb ? __ldg(s13 + static_cast<size_t>(ru / srows) * nkb + kb) : 0.f;
+        }
+        float xi = 0.f;
+        if (lane < nh) xi = exp2i(-__ldcg(ws_at<const int>(p, L.xexp) + __ldcg(ws_at<const int>(p, L.pos_tok) + pbase + lane)));
+#pragma unroll
+        for (int kb = 0; kb < kMaxH / 128; ++kb) {
+          if (kb < nkb) {
+            const int ab = use % kNacc;
+            bool ready = true;
+            if (lane == 0) ready = wait_or_abort(p, &aux.acc_full[ab], (use / kNacc) & 1, abort);
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            ++use;
+            tc::fence_after_sync();
+            if (nh > 0 && ready) {
+              const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
+              float v0[32], v1[32];
+              tc::tmem_ld32(ta, v0);
+              tc::tmem_ld32(ta + 32, v1);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                a0[j] = fmaf(sg[kb], v0[2 * j] + v0[2 * j + 1], a0[j]);
+                a0[16 + j] = fmaf(sg[kb], v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
+              }
+              tc::tmem_ld32(ta + 128, v0);
+              tc::tmem_ld32(ta + 160, v1);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                a1[j] = fmaf(su[kb], v0[2 * j] + v0[2 * j + 1], a1[j]);
+                a1[16 + j] = fmaf(su[kb], v1[2 * j] + v1[2 * j + 1], a1[16 + j]);
+              }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aux.acc_empty[ab]);
+          }
+        }
+        // SwiGLU, h rounded to bf16 (the reference's activation dtype; the shared expert is a chain
+        // of bf16 modules), then the per-(token, 128-block) absolute maxima across the 4 quarters
+        const int par = k & 1;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float xj = __shfl_sync(0xffffffffu, xi, j);
+          float h = 0.f;
+          if (j < nh) {
+            float g = a0[j] * xj, u = a1[j] * xj;
+            if (shared_tile) {
+              g = bf16_round(g);
+              u = bf16_round(u);
+              h = bf16_round(bf16_round(g * __frcp_rn(1.f + __expf(-g))) * u);
+            } else {
+              h = bf16_round(g * __frcp_rn(1.f + __expf(-g)) * u);
+            }
+          }
+          a0[j] = h;
+          const uint32_t am = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h)));
+          if (lane == j) aux.amax[par][hf][q][j] = __uint_as_float(am);
+        }
+        named_bar(kBarEpi, kEpiThreads);
+        float e2[32];
+        const int e_mine = split_exponent(fmaxf(fmaxf(aux.amax[par][hf][0][lane], aux.amax[par][hf][1][lane]),
+                                                fmaxf(aux.amax[par][hf][2][lane], aux.amax[par][hf][3][lane])));
+#pragma unroll
+        for (int j = 0; j < 32; ++j) e2[j] = exp2i(__shfl_sync(0xffffffffu, e_mine, j));
+        uint8_t* himg = p.ws + L.himg + static_cast<size_t>(2 * pbase) * p.I + kRows * rb + r;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          if (j < nh) {
+            uint16_t hi, lo;
+            split2(a0[j] * e2[j], a0[j + 1] * e2[j + 1], hi, lo);
+            himg[static_cast<size_t>(2 * j) * p.I] = static_cast<uint8_t>(hi & 0xFF);
+            himg[static_cast<size_t>(2 * j + 1) * p.I] = static_cast<uint8_t>(lo & 0xFF);
+            if (j + 1 < nh) {
+              himg[static_cast<size_t>(2 * j + 2) * p.I] = static_cast<uint8_t>(hi >> 8);
+              himg[static_cast<size_t>(2 * j + 3) * p.I] = static_cast<uint8_t>(lo >> 8);
+            }
+          }
+        }
+        if (q == 0 && lane < nh) ws_at<float>(p, L.hinv)[static_cast<size_t>(pbase + lane) * (p.I / 128) + rb] = exp2i(-e_mine);
+      } else {
+        const float* s2 = shared_tile ? p.sh_s2 : p.s2 + static_cast<size_t>(tl.x) * p.s2_stride;
+        float sd[kMaxI / 128], hv[kMaxI / 128];
+        const int ro = kRows * rb + r;
+#pragma unroll
+        for (int kb = 0; kb < kMaxI / 128; ++kb) {
+          sd[kb] = kb < nkb ? __ldg(s2 + static_cast<size_t>(ro / srows) * nkb + kb) : 0.f;
+          hv[kb] = kb < nkb && lane < nh ? __ldcg(ws_at<const float>(p, L.hinv) + static_cast<size_t>(pbase + lane) * nkb + kb) : 0.f;
+        }
+#pragma unroll
+        for (int kb = 0; kb < kMaxI / 128; ++kb) {
+          if (kb < nkb) {
+            const int ab = use % kNacc;
+            bool ready = true;
+            if (lane == 0) ready = wait_or_abort(p, &aux.acc_full[ab], (use / kNacc) & 1, abort);
+            ready = __shfl_sync(0xffffffffu, ready, 0);
+            ++use;
+            tc::fence_after_sync();
+            if (nh > 0 && ready) {
+              const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
+              float v0[32], v1[32];
+              tc::tmem_ld32(ta, v0);
+              tc::tmem_ld32(ta + 32, v1);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float c0 = sd[kb] * __shfl_sync(0xffffffffu, hv[kb], j);
+                const float c1 = sd[kb] * __shfl_sync(0xffffffffu, hv[kb], 16 + j);
+                a0[j] = fmaf(c0, v0[2 * j] + v0[2 * j + 1], a0[j]);
+                a0[16 + j] = fmaf(c1, v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
+              }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aux.acc_empty[ab]);
+          }
+        }
+        float* out = ws_at<float>(p, L.outp) + static_cast<size_t>(pbase) * p.H + kRows * rb + r;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < nh) __stcg(out + static_cast<size_t>(j) * p.H, a0[j]);
+      }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------ combine kernel
+// y = bf16(bf16(bf16(sum_j w_tj * row(t, j)) + bias) + bf16(gate_t * bf16(shared row))): the
+// rounding points of fp8_moe_forward's bf16 output, the speaker's bias add (engine.py:237) and
+// speaker_forward's bf16 tensor sum (engine.py:158). One thread per 8 outputs.
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_constant__ Params p) {
+  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const int c8 = p.H / 8;
+  const int g = blockIdx.x * kCombineThreads + threadIdx.x;
+  const int t = g / c8, n = (g % c8) * 8;
+  const bool active = t < p.T;
+  float bias[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (active && p.out_bias) {
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.out_bias + n)), b1 = __ldg(reinterpret_cast<const float4*>(p.out_bias + n + 4));
+    bias[0] = b0.x, bias[1] = b0.y, bias[2] = b0.z, bias[3] = b0.w, bias[4] = b1.x, bias[5] = b1.y, bias[6] = b1.z, bias[7] = b1.w;
+  }
+  griddep_wait();
+  griddep_launch();
+  if (!active) return;
+  const int K = p.K;
+  int pos[kMaxTopK];
+  float w[kMaxTopK];
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    pos[j] = j < K ? __ldcg(ws_at<const int>(p, L.inv) + t * K + j) : -1;
+    w[j] = j < K ? __ldcg(ws_at<const float>(p, L.pair_w) + t * K + j) : 0.f;
+  }
+  const float* outp = ws_at<const float>(p, L.outp);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    if (pos[j] >= 0) {
+      const float4* row = reinterpret_cast<const float4*>(outp + static_cast<size_t>(pos[j]) * p.H + n);
+      const float4 o0 = __ldcg(row), o1 = __ldcg(row + 1);
+      acc[0] = fmaf(w[j], o0.x, acc[0]), acc[1] = fmaf(w[j], o0.y, acc[1]), acc[2] = fmaf(w[j], o0.z, acc[2]);
+      acc[3] = fmaf(w[j], o0.w, acc[3]), acc[4] = fmaf(w[j], o1.x, acc[4]), acc[5] = fmaf(w[j], o1.y, acc[5]);
+      acc[6] = fmaf(w[j], o1.z, acc[6]), acc[7] = fmaf(w[j], o1.w, acc[7]);
+    }
+  }
+  const bool sh = p.sh_w13 != nullptr;
+  float shv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float gate = 0.f;
+  if (sh) {
+    const float4* row = reinterpret_cast<const float4*>(outp + static_cast<size_t>(p.T * K + t) * p.H + n);
+    const float4 o0 = __ldcg(row), o1 = __ldcg(row + 1);
+    shv[0] = o0.x, shv[1] = o0.y, shv[2] = o0.z, shv[3] = o0.w, shv[4] = o1.x, shv[5] = o1.y, shv[6] = o1.z, shv[7] = o1.w;
+    gate = __ldcg(ws_at<const float>(p, L.gate) + t);
+  }
+  __align__(16) __nv_bfloat16 out[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float a = bf16_round(acc[i]);
+    if (p.out_bias) a = bf16_round(a + bias[i]);
+    if (sh) a += bf16_round(gate * bf16_round(shv[i]));
+    out[i] = __float2bfloat16_rn(a);
+  }
+  *reinterpret_cast<uint4*>(p.y + static_cast<size_t>(t) * p.H + n) = *reinterpret_cast<const uint4*>(out);
+}
+
+}  // namespace pf
+
+// ------------------------------------------------------------------ host launcher
+namespace {
+
+template <typename... KArgs, typename... Args>
+int pf_launch(void (*kernel)(KArgs...), dim3 grid, int block, size_t smem, cudaStream_t stream, const char* name,
+              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) {
+    set_error(std::string(name) + " launch failed: " + cudaGetErrorString(err));
+    return 2;
+  }
+  return 0;
+}
+
+constexpr size_t kExpertSmem(bool down) {
+  return static_cast<size_t>(down ? pf::kDownStages * pf::kDownStage : pf::kUpStages * pf::kUpStage) + 1024 +
+         ((sizeof(pf::Aux) + 127) / 128) * 128;
+}
+
+}  // namespace
+
+size_t prefill_ws_bytes(int T, int H, int I, int E, int K) { return pf::layout(T, H, I, E, K).total; }
+
+// Launches the prefill chain; route = false starts at the select kernel (routing given).
+int launch_prefill(const pf::Params& p, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int sms = sm_count(dev);
+  const pf::Layout L = pf::layout(p.T, p.H, p.I, p.E, p.K);
+  static bool attrs_set = false;
+  if (!attrs_set) {
+    cudaFuncSetAttribute(pf::logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem);
+    cudaFuncSetAttribute(pf::plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(pf::expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kExpertSmem(false)));
+    cudaFuncSetAttribute(pf::expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(kExpertSmem(true)));
+    attrs_set = true;
+  }
+  const int H = p.H, I = p.I, E = p.E;
+  const uint64_t rows2 = static_cast<uint64_t>(2) * L.npos;
+  CUtensorMap mr, mx, m13, msh13, m2, msh2, mb_up[4], mb_dn[4];
+  bool ok = true;
+  if (p.mode == 1) {
+    ok = ok && tensor_map_3d(&mr, p.router_w, 2ull * H, E, 1, 2ull * H, 2ull * H * E, 128);
+    ok = ok && tensor_map_3d(&mx, p.x, 2ull * H, p.T, 1, 2ull * H, 2ull * H * p.T, pf::kLgTok);
+  }
+  ok = ok && tensor_map_3d(&m13, p.w13, H, 2ull * I, E, H, p.w13_stride, 128);
+  ok = ok && tensor_map_3d(&m2, p.w2, I, H, E, I, p.w2_stride, 128);
+  if (p.sh_w13) {
+    ok = ok && tensor_map_3d(&msh13, p.sh_w13, H, 2ull * I, 1, H, 2ull * I * H, 128);
+    ok = ok && tensor_map_3d(&msh2, p.sh_w2, I, H, 1, I, static_cast<uint64_t>(H) * I, 128);
+  } else {
+    msh13 = m13;
+    msh2 = m2;
+  }
+  for (int b = 0; b < 4; ++b) {
+    ok = ok && tensor_map_3d(&mb_up[b], p.ws + L.pimg, H, rows2, 1, H, rows2 * H, 16u << b);
+    ok = ok && tensor_map_3d(&mb_dn[b], p.ws + L.himg, I, rows2, 1, I, rows2 * I, 16u << b);
+  }
+  if (!ok) return 2;
+  int n = 0;
+  if (p.mode == 1) {
+    const dim3 g((E + pf::kRows - 1) / pf::kRows, (p.T + pf::kLgTok - 1) / pf::kLgTok, L.ks);
+    if (pf_launch(pf::logits_kernel, g, pf::kLgThreads, pf::kLgSmem, stream, "prefill logits", p, mr, mx)) return 2;
+    ++n;
+  }
+  if (pf_launch(pf::select_kernel, dim3((p.T + pf::kSelWarps - 1) / pf::kSelWarps), pf::kSelWarps * 32, 0, stream,
+                "prefill select", p))
+    return 2;
+  const size_t plan_smem = static_cast<size_t>(32 * E + E + 2 * (E + 1)) * 4;
+  if (pf_launch(pf::plan_kernel, dim3(1), pf::kPlanThreads, plan_smem, stream, "prefill plan", p)) return 2;
+  if (pf_launch(pf::dispatch_kernel, dim3((L.npos + pf::kDispatchWarps - 1) / pf::kDispatchWarps),
+                pf::kDispatchWarps * 32, 0, stream, "prefill dispatch", p))
+    return 2;
+  if (pf_launch(pf::expert_kernel<false>, dim3(sms), pf::kThreads, kExpertSmem(false), stream, "prefill up", p, m13,
+                msh13, mb_up[0], mb_up[1], mb_up[2], mb_up[3]))
+    return 2;
+  if (pf_launch(pf::expert_kernel<true>, dim3(sms), pf::kThreads, kExpertSmem(true), stream, "prefill down", p, m2,
+                msh2, mb_dn[0], mb_dn[1], mb_dn[2], mb_dn[3]))
+    return 2;
+  const int c_threads = p.T * (H / 8);
+  if (pf_launch(pf::combine_kernel, dim3((c_threads + pf::kCombineThreads - 1) / pf::kCombineThreads),
+                pf::kCombineThreads, 0, stream, "prefill combine", p))
+    return 2;
+  note_launches(n + 6);
+  return 0;
+}
+
+// Router only: logits + select (ids_out / w_out).
+int launch_route(const pf::Params& p, cudaStream_t stream) {
+  const pf::Layout L = pf::layout(p.T, p.H, p.I, p.E, p.K);
+  static bool attrs_set = false;
+  if (!attrs_set) {
+    cudaFuncSetAttribute(pf::logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem);
+    attrs_set = true;
+  }
+  CUtensorMap mr, mx;
+  if (!tensor_map_3d(&mr, p.router_w, 2ull * p.H, p.E, 1, 2ull * p.H, 2ull * p.H * p.E, 128) ||
+      !tensor_map_3d(&mx, p.x, 2ull * p.H, p.T, 1, 2ull * p.H, 2ull * p.H * p.T, pf::kLgTok))
+    return 2;
+  const dim3 g((p.E + pf::kRows - 1) / pf::kRows, (p.T + pf::kLgTok - 1) / pf::kLgTok, L.ks);
+  if (pf_launch(pf::logits_kernel, g, pf::kLgThreads, pf::kLgSmem, stream, "route logits", p, mr, mx)) return 2;
+  if (pf_launch(pf::select_kernel, dim3((p.T + pf::kSelWarps - 1) / pf::kSelWarps), pf::kSelWarps * 32, 0, stream,
+                "route select", p))
+    return 2;
+  note_launches(2);
+  return 0;
+}
+
+}  // namespace dm3
+
+// ------------------------------------------------------------------ C ABI
+namespace {
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_prefill(int T, int H, int I, int E, int top_k, const void* x, const void* w13, int64_t w13_stride,
+                  const float* s13, const void* w2, int64_t w2_stride, const float* s2, int srows, const void* y,
+                  const void* ws, size_t ws_bytes) {
+  if (T < 1) return dm3::set_error("T must be >= 1"), 1;
+  if (H < 128 || H % 128 || H > dm3::kMaxH) return dm3::set_error("H must be a multiple of 128 in [128, 2048]"), 1;
+  if (I < 128 || I % 128 || I > dm3::kMaxI) return dm3::set_error("I must be a multiple of 128 in [128, 512]"), 1;
+  if (top_k < 1 || top_k > dm3::kMaxTopK) return dm3::set_error("top_k must be in [1, 8]"), 1;
+  if (E < top_k || E > dm3::kMaxRouter) return dm3::set_error("the expert count must be in [top_k, 256]"), 1;
+  if (!x || !w13 || !s13 || !w2 || !s2 || !y || !ws) return dm3::set_error("null pointer argument"), 1;
+  if (!al16(x) || !al16(w13) || !al16(w2) || !al16(y)) return dm3::set_error("x, y and weights must be 16-byte aligned"), 1;
+  if (w13_stride % 16 || w2_stride % 16 || w13_stride < 2LL * I * H || w2_stride < static_cast<int64_t>(H) * I)
+    return dm3::set_error("expert strides must be multiples of 16 bytes covering one expert"), 1;
+  if (srows != 1 && srows != 128) return dm3::set_error("srows must be 1 or 128"), 1;
+  if (reinterpret_cast<uintptr_t>(ws) % 256) return dm3::set_error("workspace must be 256-byte aligned"), 1;
+  if (ws_bytes < dm3::prefill_ws_bytes(T, H, I, E, top_k)) return dm3::set_error("workspace too small"), 4;
+  return 0;
+}
+
+dm3::pf::Params prefill_params(const void* x, int T, int H, int I, int E, int top_k, const void* w13,
+                               int64_t w13_stride, const float* s13, int64_t s13_stride, const void* w2,
+                               int64_t w2_stride, const float* s2, int64_t s2_stride, int srows, void* y,
+                               int64_t* perm_out, int64_t* offsets_out, void* ws) {
+  dm3::pf::Params p{};
+  p.T = T;
+  p.H = H;
+  p.I = I;
+  p.E = E;
+  p.K = top_k;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.w13 = static_cast<const uint8_t*>(w13);
+  p.w13_stride = w13_stride;
+  p.s13 = s13;
+  p.s13_stride = s13_stride;
+  p.w2 = static_cast<const uint8_t*>(w2);
+  p.w2_stride = w2_stride;
+  p.s2 = s2;
+  p.s2_stride = s2_stride;
+  p.srows = srows;
+  p.sh_srows = 128;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.perm_out = perm_out;
+  p.offsets_out = offsets_out;
+  p.ws = static_cast<uint8_t*>(ws);
+  return p;
+}
+
+}  // namespace
+
+extern "C" size_t dm3_moe_prefill_workspace_bytes(int T, int H, int I, int n_experts, int top_k) {
+  if (T < 1 || H < 128 || I < 128 || n_experts < 1 || top_k < 1) return 0;
+  return dm3::prefill_ws_bytes(T, H, I, n_experts, top_k);
+}
+
+extern "C" int dm3_moe_prefill(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                               int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
+                               const float* s13, int64_t s13_stride, const void* w2, int64_t w2_stride,
+                               const float* s2, int64_t s2_stride, int srows, const void* sh_w13, const float* sh_s13,
+                               const void* sh_w2, const float* sh_s2, int sh_srows, const void* sh_gate,
+                               const float* out_bias, void* y, int64_t* ids_out, void* w_out, int64_t* perm_out,
+                               int64_t* offsets_out, void* workspace, size_t workspace_bytes, void* stream) {
+  dm3::note_launches(0);
+  int rc = check_prefill(T, H, I, n_router, top_k, x, w13, w13_stride, s13, w2, w2_stride, s2, srows, y, workspace,
+                         workspace_bytes);
+  if (rc) return rc;
+  if (!router_w || !al16(router_w)) return dm3::set_error("router weight (bf16) must be given, 16-byte aligned"), 1;
+  if (out_bias && !al16(out_bias)) return dm3::set_error("out_bias must be 16-byte aligned"), 1;
+  if (sh_w13) {
+    if (!sh_s13 || !sh_w2 || !sh_s2) return dm3::set_error("shared expert needs w13, s13, w2, s2"), 1;
+    if (!al16(sh_w13) || !al16(sh_w2)) return dm3::set_error("shared expert weights must be 16-byte aligned"), 1;
+    if (sh_srows != 1 && sh_srows != 128) return dm3::set_error("sh_srows must be 1 or 128"), 1;
+    if (sh_gate && !al16(sh_gate)) return dm3::set_error("shared gate must be 16-byte aligned"), 1;
+  }
+  dm3::pf::Params p = prefill_params(x, T, H, I, n_router, top_k, w13, w13_stride, s13, s13_stride, w2, w2_stride, s2,
+                                     s2_stride, srows, y, perm_out, offsets_out, workspace);
+  p.mode = 1;
+  p.router_w = static_cast<const __nv_bfloat16*>(router_w);
+  p.logits_bf16 = logits_bf16;
+  p.logit_bias = logit_bias;
+  p.sh_w13 = static_cast<const uint8_t*>(sh_w13);
+  p.sh_s13 = sh_s13;
+  p.sh_w2 = static_cast<const uint8_t*>(sh_w2);
+  p.sh_s2 = sh_s2;
+  p.sh_srows = sh_w13 ? sh_srows : 128;
+  p.sh_gate = sh_w13 ? static_cast<const __nv_bfloat16*>(sh_gate) : nullptr;
+  p.out_bias = out_bias;
+  p.ids_out = ids_out;
+  p.w_out = static_cast<__nv_bfloat16*>(w_out);
+  return dm3::launch_prefill(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dm3_moe_grouped(const void* x, int T, int H, int I, const int64_t* ids, const void* weights,
+                               int top_k, int n_experts, const void* w13, int64_t w13_stride, const float* s13,
+                               int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2,
+                               int64_t s2_stride, int srows, void* y, int64_t* perm_out, int64_t* offsets_out,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  dm3::note_launches(0);
+  int rc = check_prefill(T, H, I, n_experts, top_k, x, w13, w13_stride, s13, w2, w2_stride, s2, srows, y, workspace,
+                         workspace_bytes);
+  if (rc) return rc;
+  if (!ids || !weights) return dm3::set_error("ids and weights are required"), 1;
+  dm3::pf::Params p = prefill_params(x, T, H, I, n_experts, top_k, w13, w13_stride, s13, s13_stride, w2, w2_stride, s2,
+                                     s2_stride, srows, y, perm_out, offsets_out, workspace);
+  p.mode = 0;
+  p.ids = ids;
+  p.rw = static_cast<const __nv_bfloat16*>(weights);
+  return dm3::launch_prefill(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t dm3_route_workspace_bytes(int T, int H, int n_router, int top_k) {
+  if (T < 1 || H < 128 || n_router < 1 || top_k < 1) return 0;
+  return dm3::pf::layout(T, H, 128, n_router, top_k).pos_tok;
+}
+
+extern "C" int dm3_route(const void* x, int T, int H, const void* router_w, int n_router, int top_k, int logits_bf16,
+                         const float* logit_bias, int64_t* ids_out, void* w_out, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  dm3::note_launches(0);
+  if (T < 1) return dm3::set_error("T must be >= 1"), 1;
+  if (H < 128 || H % 128 || H > dm3::kMaxH) return dm3::set_error("H must be a multiple of 128 in [128, 2048]"), 1;
+  if (top_k < 1 || top_k > dm3::kMaxTopK) return dm3::set_error("top_k must be in [1, 8]"), 1;
+  if (n_router < top_k || n_router > dm3::kMaxRouter) return dm3::set_error("n_router must be in [top_k, 256]"), 1;
+  if (!x || !router_w || !ids_out || !w_out || !workspace) return dm3::set_error("null pointer argument"), 1;
+  if (!al16(x) || !al16(router_w)) return dm3::set_error("x and router weight must be 16-byte aligned"), 1;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256) return dm3::set_error("workspace must be 256-byte aligned"), 1;
+  if (workspace_bytes < dm3_route_workspace_bytes(T, H, n_router, top_k)) return dm3::set_error("workspace too small"), 4;
+  dm3::pf::Params p{};
+  p.T = T;
+  p.H = H;
+  p.I = 128;
+  p.E = n_router;
+  p.K = top_k;
+  p.mode = 1;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.router_w = static_cast<const __nv_bfloat16*>(router_w);
+  p.logits_bf16 = logits_bf16;
+  p.logit_bias = logit_bias;
+  p.ids_out = ids_out;
+  p.w_out = static_cast<__nv_bfloat16*>(w_out);
+  p.ws = static_cast<uint8_t*>(workspace);
+  return dm3::launch_route(p, static_cast<cudaStream_t>(stream));
+}

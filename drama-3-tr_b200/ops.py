@@ -11,6 +11,9 @@ Ops:
                      (fish-speech fp8_moe_forward, engine.py:147, :236)
   dm3::moe_layer     fused decode MoE layer: router + top-k + experts + shared expert + bias
                      (engine.py:153-158, :232-237)
+  dm3::moe_prefill   prompt-reading MoE layer over T tokens: router, dispatch permutation, grouped
+                     tensor-core SwiGLU, combine, shared expert (engine.py:143-147, :153-158)
+  dm3::route         the router alone: softmax / top-k / renormalise (engine.py:233-235)
 """
 
 from __future__ import annotations
@@ -28,6 +31,7 @@ BF16 = torch.bfloat16
 MAX_ROWS = 4  # rows per launch of the skinny kernels
 
 _workspaces: dict = {}
+_pf_workspaces: dict = {}
 
 
 def _ptr(t: Optional[Tensor]):
@@ -77,6 +81,22 @@ def moe_workspace(device: torch.device, H: int, I: int) -> Tensor:
         nbytes = _lib.load().dm3_moe_workspace_bytes(MAX_ROWS, H, I)
         ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
         _workspaces[key] = ws
+    return ws
+
+
+def prefill_workspace(device: torch.device, nbytes: int) -> Tensor:
+    """A zero-initialised scratch of at least nbytes for the prefill kernels on one device, grown
+    on demand and shared by calls issued in stream order (the kernels rewrite what they read)."""
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _pf_workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError(
+                "drama3_b200: the prefill workspace must be created before CUDA-graph capture; run the op once "
+                "at the largest size first")
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _pf_workspaces[key] = ws
     return ws
 
 
@@ -159,8 +179,15 @@ def moe_forward(x: Tensor, ids: Tensor, weights: Tensor, w13: Tensor, s13: Tenso
     weights = weights.to(BF16).contiguous()
     k = ids.shape[1]
     y = torch.empty((T, H), dtype=BF16, device=x.device)
-    ws = moe_workspace(x.device, H, I)
     st = _stream(x.device)
+    if T > MAX_ROWS:
+        # many rows: the grouped tensor-core path (dispatch by expert, one pass over each expert)
+        ws = prefill_workspace(x.device, lib.dm3_moe_prefill_workspace_bytes(T, H, I, E, k))
+        rc = lib.dm3_moe_grouped(_ptr(x), T, H, I, _ptr(ids), _ptr(weights), k, E, _ptr(w13), w13s, _ptr(s13), s13s,
+                                 _ptr(w2), w2s, _ptr(s2), s2s, srows, _ptr(y), None, None, _ptr(ws), ws.numel(), st)
+        _lib.check(rc, "dm3_moe_grouped")
+        return y
+    ws = moe_workspace(x.device, H, I)
     for t0 in range(0, T, MAX_ROWS):
         t = min(MAX_ROWS, T - t0)
         rc = lib.dm3_moe_forward(_ptr(x[t0:]), t, H, I, _ptr(ids[t0:]), _ptr(weights[t0:]), k, E, _ptr(w13), w13s,
@@ -228,3 +255,96 @@ def _(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_
     T = x.shape[0]
     return (torch.empty_like(x, dtype=BF16), x.new_empty((T, top_k), dtype=torch.int64),
             x.new_empty((T, top_k), dtype=BF16))
+
+
+# ----------------------------------------------------------------------------- moe_prefill
+def _shared_args(sh_w13, sh_s13, sh_w2, sh_s2, H: int, I: int):
+    sh_srows = 128
+    if sh_w13 is not None:
+        sh_w13, sh_w2 = _fp8_bytes(sh_w13).contiguous(), _fp8_bytes(sh_w2).contiguous()
+        sh_s13, sh_s2 = sh_s13.contiguous(), sh_s2.contiguous()
+        if tuple(sh_w13.shape) != (2 * I, H) or tuple(sh_w2.shape) != (H, I):
+            raise RuntimeError("shared expert must be w13 [2I, H], w2 [H, I]")
+        sh_srows = scale_rows(2 * I, sh_s13.shape[0])
+        if scale_rows(H, sh_s2.shape[0]) != sh_srows:
+            raise RuntimeError("shared expert s13 and s2 must use the same scale layout")
+    return sh_w13, sh_s13, sh_w2, sh_s2, sh_srows
+
+
+@torch.library.custom_op("dm3::moe_prefill", mutates_args=())
+def moe_prefill(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, logit_bias: Optional[Tensor],
+                w13: Tensor, s13: Tensor, w2: Tensor, s2: Tensor, sh_w13: Optional[Tensor], sh_s13: Optional[Tensor],
+                sh_w2: Optional[Tensor], sh_s2: Optional[Tensor], sh_gate: Optional[Tensor],
+                out_bias: Optional[Tensor]) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Prompt-reading MoE layer over T tokens in one chain of launches. Returns (y bf16 [T, H],
+    ids int64 [T, k], routing weights bf16 [T, k], dispatch permutation int64 [T * k] (pair indices
+    t * k + j stably sorted by expert), per-expert offsets int64 [E + 1])."""
+    _require_cuda(x, router_w, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias)
+    lib = _lib.load()
+    w13, w2 = _fp8_bytes(w13), _fp8_bytes(w2)
+    x = x.contiguous()
+    T, H = x.shape
+    E, I, srows, w13s, s13s, w2s, s2s = _expert_strides(w13, s13, w2, s2, H)
+    if router_w.dtype != BF16 or tuple(router_w.shape) != (E, H):
+        raise RuntimeError("the prefill router weight must be bf16 [E, H] matching the experts")
+    router_w = router_w.contiguous()
+    if logit_bias is not None:
+        logit_bias = logit_bias.float().contiguous()
+    sh_w13, sh_s13, sh_w2, sh_s2, sh_srows = _shared_args(sh_w13, sh_s13, sh_w2, sh_s2, H, I)
+    if sh_gate is not None:
+        sh_gate = sh_gate.to(BF16).reshape(-1).contiguous()
+    if out_bias is not None:
+        out_bias = out_bias.float().contiguous()
+    dev = x.device
+    y = torch.empty((T, H), dtype=BF16, device=dev)
+    ids = torch.empty((T, top_k), dtype=torch.int64, device=dev)
+    wts = torch.empty((T, top_k), dtype=BF16, device=dev)
+    perm = torch.empty((T * top_k,), dtype=torch.int64, device=dev)
+    offsets = torch.empty((E + 1,), dtype=torch.int64, device=dev)
+    ws = prefill_workspace(dev, lib.dm3_moe_prefill_workspace_bytes(T, H, I, E, top_k))
+    rc = lib.dm3_moe_prefill(_ptr(x), T, H, I, _ptr(router_w), E, top_k, 1 if logits_bf16 else 0, _ptr(logit_bias),
+                             _ptr(w13), w13s, _ptr(s13), s13s, _ptr(w2), w2s, _ptr(s2), s2s, srows, _ptr(sh_w13),
+                             _ptr(sh_s13), _ptr(sh_w2), _ptr(sh_s2), sh_srows, _ptr(sh_gate), _ptr(out_bias), _ptr(y),
+                             _ptr(ids), _ptr(wts), _ptr(perm), _ptr(offsets), _ptr(ws), ws.numel(), _stream(dev))
+    _lib.check(rc, "dm3_moe_prefill")
+    return y, ids, wts, perm, offsets
+
+
+@moe_prefill.register_fake
+def _(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias):
+    T = x.shape[0]
+    E = w13.shape[0]
+    return (torch.empty_like(x, dtype=BF16), x.new_empty((T, top_k), dtype=torch.int64),
+            x.new_empty((T, top_k), dtype=BF16), x.new_empty((T * top_k,), dtype=torch.int64),
+            x.new_empty((E + 1,), dtype=torch.int64))
+
+
+# ----------------------------------------------------------------------------- route
+@torch.library.custom_op("dm3::route", mutates_args=())
+def route(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool,
+          logit_bias: Optional[Tensor]) -> tuple[Tensor, Tensor]:
+    """softmax(x @ router_w.T (+ bias)) -> top-k -> renormalise -> bf16 for T tokens (bf16 router).
+    Returns (ids int64 [T, k] by descending probability, weights bf16 [T, k])."""
+    _require_cuda(x, router_w, logit_bias)
+    lib = _lib.load()
+    x = x.contiguous()
+    T, H = x.shape
+    if router_w.dtype != BF16 or router_w.shape[1] != H:
+        raise RuntimeError("router weight must be bf16 [E, H]")
+    router_w = router_w.contiguous()
+    E = router_w.shape[0]
+    if logit_bias is not None:
+        logit_bias = logit_bias.float().contiguous()
+    ids = torch.empty((T, top_k), dtype=torch.int64, device=x.device)
+    wts = torch.empty((T, top_k), dtype=BF16, device=x.device)
+    ws = prefill_workspace(x.device, lib.dm3_route_workspace_bytes(T, H, E, top_k))
+    rc = lib.dm3_route(_ptr(x), T, H, _ptr(router_w), E, top_k, 1 if logits_bf16 else 0, _ptr(logit_bias), _ptr(ids),
+                       _ptr(wts), _ptr(ws), ws.numel(), _stream(x.device))
+    _lib.check(rc, "dm3_route")
+    return ids, wts
+
+
+@route.register_fake
+def _(x, router_w, top_k, logits_bf16, logit_bias):
+    T = x.shape[0]
+    return x.new_empty((T, top_k), dtype=torch.int64), x.new_empty((T, top_k), dtype=BF16)

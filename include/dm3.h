@@ -159,6 +159,61 @@ int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const void* router
                           const float* sh_s2, int sh_srows, const void* sh_gate, const float* out_bias, void* y,
                           int64_t* ids_out, void* w_out, void* stream);
 
+/*
+ * Workspace bytes of dm3_moe_prefill / dm3_moe_grouped for T tokens, hidden H, intermediate I,
+ * n_experts routed experts and top_k. Allocate it zero-filled once; every call rewrites what it
+ * reads, so it can be reused by later calls on the same stream with the same or smaller sizes.
+ */
+size_t dm3_moe_prefill_workspace_bytes(int T, int H, int I, int n_experts, int top_k);
+
+/*
+ * Prompt-reading (prefill) MoE layer for T tokens, the routed path of SparseMoeBlock.forward
+ * that speaker_forward falls back to when more rows than OnDemandExperts.batch arrive
+ * (engine.py:153-157): a bf16 router over n_router experts (+ optional fp32 logit bias) with
+ * softmax, top-k and renormalisation to bf16 (exp1_routing.py:59-60, engine.py:233-235), the
+ * token-to-expert dispatch that OnDemandExperts.forward prepares with ids.unique() / slot_map
+ * (engine.py:143-146), the grouped block-FP8 SwiGLU of fp8_moe_forward (engine.py:147), the
+ * weighted combine and the sigmoid-gated shared expert (engine.py:158), and an optional fp32 bias.
+ * Arguments as dm3_moe_layer (router_w bf16 [n_router, H], experts with their dim-0 strides), plus:
+ *   perm_out     optional int64 [T * top_k]: the (token, k) pairs (index t * top_k + j) in dispatch
+ *                order, i.e. stably sorted by expert (argsort(ids.flatten(), stable=True))
+ *   offsets_out  optional int64 [n_router + 1]: first dispatch position of each expert
+ * Router logits are those of exact sums rounded once (fp32, then bf16 for logits_bf16), so the
+ * chosen experts match an exact reference; ties go to the lower expert index.
+ * 1 <= T, H % 128 == 0, H <= 2048, I % 128 == 0, I <= 512, top_k <= n_router <= 256, top_k <= 8.
+ */
+int dm3_moe_prefill(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                    int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride, const float* s13,
+                    int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride,
+                    int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
+                    int sh_srows, const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
+                    int64_t* perm_out, int64_t* offsets_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * fp8_moe_forward(x, ids, weights, w13, s13, w2, s2) for any row count (engine.py:147, :236): the
+ * dispatch, grouped SwiGLU and combine of dm3_moe_prefill with the caller's routing. Arguments as
+ * dm3_moe_forward plus perm_out / offsets_out as dm3_moe_prefill; the workspace is
+ * dm3_moe_prefill_workspace_bytes(T, H, I, n_experts, top_k). Out-of-range ids are skipped and
+ * flagged in the status word (dm3_moe_status).
+ */
+int dm3_moe_grouped(const void* x, int T, int H, int I, const int64_t* ids, const void* weights, int top_k,
+                    int n_experts, const void* w13, int64_t w13_stride, const float* s13, int64_t s13_stride,
+                    const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride, int srows, void* y,
+                    int64_t* perm_out, int64_t* offsets_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes of dm3_route for T tokens, hidden H, n_router experts and top_k. */
+size_t dm3_route_workspace_bytes(int T, int H, int n_router, int top_k);
+
+/*
+ * The router alone for T tokens: logits = x @ router_w.T (bf16 [n_router, H], exact sums rounded
+ * once; rounded to bf16 for logits_bf16) + optional fp32 logit_bias, softmax, top-k, renormalised
+ * bf16 weights (exp1_routing.py:59-60, engine.py:233-235). ids_out int64 [T, top_k] in descending
+ * probability, w_out bf16 [T, top_k]. Limits as dm3_moe_prefill.
+ */
+int dm3_route(const void* x, int T, int H, const void* router_w, int n_router, int top_k, int logits_bf16,
+              const float* logit_bias, int64_t* ids_out, void* w_out, void* workspace, size_t workspace_bytes,
+              void* stream);
+
 /* Number of kernels the last MoE / GEMV entry point launched on this host thread. */
 int dm3_last_launch_count(void);
 

@@ -34,3 +34,27 @@ def experts(e: int, h: int, i: int, seed: int, srows: int = 128):
 
 def to_dev(d: dict, dev="cuda"):
     return {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
+
+
+def routed_layer(seed, srows=128, shared=True, h=2048, i=512, e=256):
+    """Seeded routed layer: block-FP8 experts, a bf16 router and optionally a shared expert
+    with its bf16 gate row."""
+    from tests.golden import inputs
+
+    ex = experts(e, h, i, seed=seed, srows=srows)
+    gate = inputs.router256(seed + 1, e=e, h=h)
+    out = {"experts": ex, "gate": gate}
+    if shared:
+        sw = experts(1, h, i, seed=seed + 2, srows=srows)
+        out["sh"] = {k: v[0] for k, v in sw.items()}
+        out["sh_gate"] = inputs.shared_gate_weight(seed + 3, h=h)
+    return out
+
+
+def oracle_shared(layer, srows):
+    """The shared expert as the oracle's (q, s, srows) gate / up / down triples."""
+    sh = layer["sh"]
+    i = sh["w2"].shape[1]
+    k = i // srows  # scale rows covering the gate half of w13
+    return {"gate": (sh["w13"][:i], sh["s13"][:k], srows), "up": (sh["w13"][i:], sh["s13"][k:], srows),
+            "down": (sh["w2"], sh["s2"], srows)}

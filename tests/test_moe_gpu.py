@@ -9,7 +9,7 @@ import torch
 
 import oracle
 from tests.golden import inputs
-from tests.helpers import REL_L2_TOL, experts, rel_l2, to_dev
+from tests.helpers import REL_L2_TOL, experts, oracle_shared as _oracle_shared, rel_l2, routed_layer as _routed_layer, to_dev
 
 pytestmark = pytest.mark.gpu
 G = Path(__file__).resolve().parent / "golden"
@@ -113,25 +113,6 @@ def test_speaker_matches_reference_golden(dm3, spk):
         assert np.array_equal(ids.cpu().numpy(), g[f"ids_t{t}"])
         ref = torch.from_numpy(g[f"y_t{t}"]).view(torch.bfloat16)
         assert rel_l2(y, ref) < 5e-3
-
-
-def _routed_layer(seed, srows=128, shared=True, h=H, i=I, e=256):
-    ex = experts(e, h, i, seed=seed, srows=srows)
-    gate = inputs.router256(seed + 1, e=e, h=h)
-    out = {"experts": ex, "gate": gate}
-    if shared:
-        sw = experts(1, h, i, seed=seed + 2, srows=srows)
-        out["sh"] = {k: v[0] for k, v in sw.items()}
-        out["sh_gate"] = inputs.shared_gate_weight(seed + 3, h=h)
-    return out
-
-
-def _oracle_shared(layer, srows):
-    sh = layer["sh"]
-    i = sh["w2"].shape[1]
-    k = i // srows  # scale rows covering the gate half of w13
-    return {"gate": (sh["w13"][:i], sh["s13"][:k], srows), "up": (sh["w13"][i:], sh["s13"][k:], srows),
-            "down": (sh["w2"], sh["s2"], srows)}
 
 
 @pytest.mark.parametrize("srows", [128, 1])
