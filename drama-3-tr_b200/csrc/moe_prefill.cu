@@ -47,19 +47,15 @@ constexpr int kSlab = kRows * 128;           // one 128-byte K slab of a 128-row
 constexpr int kThreads = 320;                // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kUpStages = 4, kDownStages = 6;
-constexpr int kUpStage = 3 * kSlab;          // gate slab, up slab, activation slab (<= 128 rows)
-constexpr int kDownStage = 2 * kSlab;        // weight slab, activation slab
-constexpr int kUpAcc = 2, kDownAcc = 4;      // TMEM accumulator buffers (256 / 128 columns each)
+constexpr int kStages = 4;                   // ring of TMA stages
+constexpr int kStage = 3 * kSlab;            // two weight slabs, the activation slab (<= 128 rows)
+constexpr int kNacc = 2;                     // TMEM accumulator buffers of 256 columns
 constexpr int kLgK = 512;                    // K per logits CTA
 constexpr int kLgSlabs = kLgK / 64;          // 64 bf16 per 128-byte slab
 constexpr int kLgTok = 32;                   // tokens per logits CTA (N)
 constexpr int kLgThreads = 192;              // warp 0 TMA + MMA, warp 1 TMEM, warps 2-5 epilogue
 constexpr int kLgBSlab = kLgTok * 128;
 constexpr int kLgSmem = kLgSlabs * (kSlab + kLgBSlab) + 1024 + 256;
-constexpr int kSelWarps = 8;
-constexpr int kPlanThreads = 1024;
-constexpr int kDispatchWarps = 8;
 constexpr int kCombineThreads = 256;
 constexpr int kBarEpi = 1;                   // named barrier of the up epilogue's warps
 
@@ -103,7 +99,7 @@ struct Params {
 // Positions: the P = T * K routed (token, k) pairs in dispatch order (expert-major, stable), then
 // one position per token for the shared expert. Every per-position buffer is indexed by position.
 struct Layout {
-  size_t ctrl, lpart, wnorm, pair_e, pair_w, gate, xexp, pos_tok, perm, inv, tiles, pimg, himg, hinv, outp, total;
+  size_t ctrl, lpart, wnorm, pair_e, pair_w, gate, xexp, pos_tok, pxinv, perm, inv, tiles, pimg, himg, hinv, outp, total;
   int ks, max_tiles, npos;
 };
 
@@ -132,6 +128,8 @@ __host__ __device__ inline Layout layout(int T, int H, int I, int E, int K) {
   L.xexp = o = aup(o, 128);
   o += static_cast<size_t>(T) * 4;
   L.pos_tok = o = aup(o, 128);
+  o += static_cast<size_t>(L.npos) * 4;
+  L.pxinv = o = aup(o, 128);  // [npos] 2^-e of the position's token split
   o += static_cast<size_t>(L.npos) * 4;
   L.perm = o = aup(o, 128);
   o += P * 4;
@@ -162,7 +160,7 @@ __device__ __forceinline__ void flag(const Params& p, uint32_t bits) {
 // Waits unless the CTA has aborted; a wait that runs out aborts the CTA (and reports it once).
 __device__ __forceinline__ bool wait_or_abort(const Params& p, uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (*abort) return false;
-  if (mbar_wait(bar, parity)) return true;
+  if (mbar_wait_sleep(bar, parity)) return true;
   if (!*abort) flag(p, STATUS_TIMEOUT);
   *abort = 1;
   return false;
@@ -228,28 +226,33 @@ __global__ void __launch_bounds__(kLgThreads, 1)
   } else if (warp >= 2) {
     const int q = warp & 3;
     const int r = 32 * q + lane;
-    if (blockIdx.y == 0) {
-      // squared norm of router row m0 + r over this k range (the slab swizzle only permutes
-      // 16-byte chunks inside the row's 128 bytes)
-      float n2 = 0.f;
-      for (int s = 0; s < nsl; ++s) {
-        if (!mbar_wait(&full[s], 0)) {
-          flag(p, STATUS_TIMEOUT);
-          break;
-        }
-        const uint4* row = reinterpret_cast<const uint4*>(sa + s * kSlab + (r >> 3) * 1024 + (r & 7) * 128);
+    // squared norms of this CTA's share of the 128 router rows over this k range (the token-tile
+    // CTAs split the rows; 16 threads per row; the slab swizzle only permutes 16-byte chunks
+    // inside a row's 128 bytes)
+    const int rp = (kRows + gridDim.y - 1) / gridDim.y;
+    const int r_lo = blockIdx.y * rp, r_hi = min(kRows, r_lo + rp);
+    if (r_lo < r_hi) {
+      bool landed = true;
+      for (int s = 0; s < nsl && landed; ++s) landed = mbar_wait(&full[s], 0);
+      if (!landed && r == 0) flag(p, STATUS_TIMEOUT);
+      for (int base = r_lo; base < r_hi; base += 8) {
+        const int row = base + (r >> 4), part = r & 15;
+        float n2 = 0.f;
+        if (landed && row < r_hi) {
+          for (int ci = part; ci < nsl * 8; ci += 16) {
+            const uint4 v = *reinterpret_cast<const uint4*>(sa + (ci >> 3) * kSlab + (row >> 3) * 1024 + (row & 7) * 128 + (ci & 7) * 16);
+            const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 v = row[c];
-          const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float f = __bfloat162float(e[i]);
-            n2 = fmaf(f, f, n2);
+            for (int i = 0; i < 8; ++i) {
+              const float f = __bfloat162float(e[i]);
+              n2 = fmaf(f, f, n2);
+            }
           }
         }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+        if (part == 0 && row < r_hi && m0 + row < p.E) ws_at<float>(p, L.wnorm)[ks * p.E + m0 + row] = n2;
       }
-      if (m0 + r < p.E) ws_at<float>(p, L.wnorm)[ks * p.E + m0 + r] = n2;
     }
     const bool ready = mbar_wait(done, 0);
     if (!ready && lane == 0) flag(p, STATUS_TIMEOUT);
@@ -271,30 +274,21 @@ __global__ void __launch_bounds__(kLgThreads, 1)
 }
 
 // ------------------------------------------------------------------ select kernel
-constexpr int kXC = kMaxH / 256;  // 8-element chunks of a token row per lane
+constexpr int kSelThreads = 256;  // one CTA per token; thread e owns expert e, 8 elements of x
+constexpr int kSelChunk = 8;      // candidate rows fetched together
+constexpr int kMaxKs = (kMaxH + kLgK - 1) / kLgK;
 
-// The router logit of expert e as the reference's oracle defines it: the exact sum of the bf16
-// products (fp64 accumulation of exact fp64 products; 2048 terms keep it within 2^-42 of exact),
-// rounded once to fp32. The whole warp returns the same value.
-__device__ __forceinline__ float exact_dot(const uint4 (&xv)[kXC], const __nv_bfloat16* wrow, int H, int lane) {
-  double acc[4] = {0.0, 0.0, 0.0, 0.0};
-#pragma unroll
-  for (int i = 0; i < kXC; ++i) {
-    const int k = 256 * i + 8 * lane;
-    if (k < H) {
-      const uint4 w = __ldg(reinterpret_cast<const uint4*>(wrow + k));
-      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&w);
-      const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        acc[j & 3] = fma(static_cast<double>(__bfloat162float(xe[j])), static_cast<double>(__bfloat162float(we[j])), acc[j & 3]);
-    }
-  }
-  double s = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  return __double2float_rn(s);
-}
+struct SelSmem {
+  double part[kSelThreads / 32][kSelChunk];
+  uint64_t keys[kMaxRouter];
+  float fx[kMaxRouter];
+  int cand[kMaxRouter + 1];
+  uint8_t is_cand[kMaxRouter];
+  float red[2][kSelThreads / 32];
+  int wcount[kSelThreads / 32];
+  float theta, gcoef;
+  int ncand;
+};
 
 // The logit the softmax sees: fp32 (or rounded to bf16 for a bf16 router) + the optional bias.
 // Non-decreasing in v, so bounds on v give bounds on it.
@@ -304,30 +298,33 @@ __device__ __forceinline__ float logit_map(const Params& p, float v, int e) {
   return v;
 }
 
-// One warp per token. Routing given (mode 0): validates the ids and records the pairs. Router
+// One CTA per token. Routing given (mode 0): validates the ids and records the pairs. Router
 // (mode 1): approximate logit a_e = sum of the logits kernel's partials; its error is below
 // d_e = 2^-10 |x| |w_e| (the fp32 tensor-core sums err by far less than 2^-16 of sum |x_k w_ek|,
 // which Cauchy-Schwarz bounds by |x| |w_e|). theta = the k-th largest of map(a_e - d_e); an expert
 // with map(a_e + d_e) < theta has k experts strictly above it and cannot be selected, every other
-// one is a candidate whose logit is recomputed exactly. Selection, softmax and renormalisation then
-// follow the decode router (ties to the lower index), with the exact values of every candidate;
-// the softmax denominator takes the approximate values of the others, whose share cancels in the
+// one is a candidate whose logit is recomputed exactly: the exact bf16 products summed in fp64
+// (within 2^-42 of exact for 2048 terms) and rounded once to fp32, as the oracle's float64 matmul.
+// Candidate rows are fetched kSelChunk at a time by the whole CTA (8 elements per thread), so a
+// chunk costs one memory round trip. Selection, softmax and renormalisation follow the decode
+// router (ties to the lower index) with the exact values of every candidate; the softmax
+// denominator takes the approximate values of the others, whose share cancels in the
 // renormalised weights.
-__global__ void __launch_bounds__(kSelWarps * 32) select_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_constant__ Params p) {
+  __shared__ SelSmem sm;
   const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * kSelWarps + warp;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x;
+  const int H = p.H, E = p.E, K = p.K;
   griddep_wait();
   griddep_launch();
-  if (t >= p.T) return;
-  const int H = p.H, E = p.E, K = p.K;
-  uint4 xv[kXC];
+  // this thread's 8 elements of the token row, |x|^2 and max |x|
+  const bool xin = 8 * tid < H;
+  const uint4 xv = xin ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * H + 8 * tid))
+                       : make_uint4(0u, 0u, 0u, 0u);
   float xn2 = 0.f, xm = 0.f;
-#pragma unroll
-  for (int i = 0; i < kXC; ++i) {
-    const int k = 256 * i + 8 * lane;
-    xv[i] = k < H ? __ldg(reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * H + k)) : make_uint4(0u, 0u, 0u, 0u);
-    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv[i]);
+  {
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float f = __bfloat162float(xe[j]);
@@ -335,73 +332,142 @@ __global__ void __launch_bounds__(kSelWarps * 32) select_kernel(const __grid_con
       xm = fmaxf(xm, fabsf(f));
     }
   }
+  // approximate logit of expert tid (all partials requested before the reductions)
+  float a = 0.f, w2 = 0.f;
+  if (p.mode == 1 && tid < E) {
+    float ap[kMaxKs], wp[kMaxKs];
+#pragma unroll
+    for (int s = 0; s < kMaxKs; ++s) {
+      ap[s] = s < L.ks ? __ldcg(ws_at<const float>(p, L.lpart) + (static_cast<size_t>(s) * p.T + t) * E + tid) : 0.f;
+      wp[s] = s < L.ks ? __ldcg(ws_at<const float>(p, L.wnorm) + s * E + tid) : 0.f;
+    }
+#pragma unroll
+    for (int s = 0; s < kMaxKs; ++s) {
+      a += ap[s];
+      w2 += wp[s];
+    }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     xn2 += __shfl_xor_sync(0xffffffffu, xn2, o);
     xm = fmaxf(xm, __shfl_xor_sync(0xffffffffu, xm, o));
   }
-  if (lane == 0) ws_at<int>(p, L.xexp)[t] = split_exponent(xm);
+  if (lane == 0) {
+    sm.red[0][warp] = xn2;
+    sm.red[1][warp] = xm;
+  }
+  __syncthreads();
+  xn2 = 0.f;
+  xm = 0.f;
+#pragma unroll
+  for (int w = 0; w < kSelThreads / 32; ++w) {
+    xn2 += sm.red[0][w];
+    xm = fmaxf(xm, sm.red[1][w]);
+  }
+  if (tid == 0) ws_at<int>(p, L.xexp)[t] = split_exponent(xm);
   int* pair_e = ws_at<int>(p, L.pair_e) + t * K;
   float* pair_w = ws_at<float>(p, L.pair_w) + t * K;
   if (p.mode == 0) {
-    if (lane < K) {
-      const int64_t id = p.ids[t * K + lane];
+    if (tid < K) {
+      const int64_t id = p.ids[t * K + tid];
       const bool ok = id >= 0 && id < E;
       if (!ok) flag(p, STATUS_BAD_EXPERT);
-      pair_e[lane] = ok ? static_cast<int>(id) : -1;
-      pair_w[lane] = __bfloat162float(p.rw[t * K + lane]);
+      pair_e[tid] = ok ? static_cast<int>(id) : -1;
+      pair_w[tid] = __bfloat162float(p.rw[t * K + tid]);
     }
-    if (lane == 0) ws_at<float>(p, L.gate)[t] = 1.f;
+    if (tid == 0) ws_at<float>(p, L.gate)[t] = 1.f;
     return;
   }
-  // approximate logits and their windows
-  float fx[8], fu[8];
-  uint64_t dk[8];
-  const float* lp = ws_at<const float>(p, L.lpart);
-  const float* wn = ws_at<const float>(p, L.wnorm);
+  // windows and the threshold
+  float fu = -FLT_MAX;
+  if (tid < E) {
+    const float d = __fmul_ru(ldexpf(sqrtf(xn2 * w2), -10), 1.001f) + 1e-30f;
+    sm.fx[tid] = logit_map(p, a, tid);
+    fu = logit_map(p, __fadd_ru(a, d), tid);
+    sm.keys[tid] = (static_cast<uint64_t>(order_key(logit_map(p, __fsub_rd(a, d), tid))) << 32) | static_cast<uint32_t>(~tid);
+  } else if (tid < kMaxRouter) {
+    sm.keys[tid] = 0ull;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t k8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) k8[i] = sm.keys[lane + 32 * i];
+    warp_top8(k8);
+    uint64_t kth = k8[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j)
+      if (j == K - 1) kth = k8[j];
+    if (lane == 0) sm.theta = key_value(static_cast<uint32_t>(kth >> 32));
+  }
+  __syncthreads();
+  // candidate list (ascending expert order), then the shared gate row
+  const bool cand = tid < E && fu >= sm.theta;
+  const unsigned bal = __ballot_sync(0xffffffffu, cand);
+  if (lane == 0) sm.wcount[warp] = __popc(bal);
+  if (tid < kMaxRouter) sm.is_cand[tid] = cand ? 1 : 0;
+  __syncthreads();
+  int before = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kSelThreads / 32; ++w) {
+    before += w < warp ? sm.wcount[w] : 0;
+    total += sm.wcount[w];
+  }
+  if (cand) sm.cand[before + __popc(bal & ((1u << lane) - 1u))] = tid;
+  const bool gate_row = p.sh_gate != nullptr;
+  if (tid == 0) {
+    if (gate_row) sm.cand[total] = E;  // the shared expert's gate row
+    sm.ncand = total + (gate_row ? 1 : 0);
+  }
+  __syncthreads();
+  const int nc = sm.ncand;
+  for (int c0 = 0; c0 < nc; c0 += kSelChunk) {
+    uint4 wv[kSelChunk];
+#pragma unroll
+    for (int c = 0; c < kSelChunk; ++c) {
+      wv[c] = make_uint4(0u, 0u, 0u, 0u);
+      if (c0 + c < nc && xin) {
+        const int row = sm.cand[c0 + c];
+        const __nv_bfloat16* wr = row < E ? p.router_w + static_cast<size_t>(row) * H : p.sh_gate;
+        wv[c] = __ldg(reinterpret_cast<const uint4*>(wr + 8 * tid));
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kSelChunk; ++c) {
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[c]);
+      const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+      double acc = 0.0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        acc = fma(static_cast<double>(__bfloat162float(xe[j])), static_cast<double>(__bfloat162float(we[j])), acc);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) sm.part[warp][c] = acc;
+    }
+    __syncthreads();
+    if (tid < kSelChunk && c0 + tid < nc) {
+      double sum = 0.0;
+#pragma unroll
+      for (int w = 0; w < kSelThreads / 32; ++w) sum += sm.part[w][tid];
+      const float v = __double2float_rn(sum);
+      const int row = sm.cand[c0 + tid];
+      if (row < E)
+        sm.fx[row] = logit_map(p, v, row);
+      else
+        sm.gcoef = bf16_round(1.f / (1.f + expf(-bf16_round(v))));
+    }
+    __syncthreads();
+  }
+  if (warp != 0) return;
+  // selection among the candidates (exact values), softmax over all, renormalise
+  float fx[8];
+  uint64_t k[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = lane + 32 * i;
-    fx[i] = fu[i] = -FLT_MAX;
-    dk[i] = 0ull;
-    if (e < E) {
-      float a = 0.f, w2 = 0.f;
-      for (int s = 0; s < L.ks; ++s) {
-        a += __ldcg(lp + (static_cast<size_t>(s) * p.T + t) * E + e);
-        w2 += __ldcg(wn + s * E + e);
-      }
-      const float d = __fmul_ru(ldexpf(sqrtf(xn2 * w2), -10), 1.001f) + 1e-30f;
-      fx[i] = logit_map(p, a, e);
-      fu[i] = logit_map(p, __fadd_ru(a, d), e);
-      dk[i] = (static_cast<uint64_t>(order_key(logit_map(p, __fsub_rd(a, d), e))) << 32) | static_cast<uint32_t>(~e);
-    }
+    fx[i] = e < E ? sm.fx[e] : -FLT_MAX;
+    k[i] = (e < E && sm.is_cand[e]) ? (static_cast<uint64_t>(order_key(fx[i])) << 32) | static_cast<uint32_t>(~e) : 0ull;
   }
-  warp_top8(dk);
-  uint64_t kth = dk[0];
-#pragma unroll
-  for (int j = 1; j < 8; ++j)
-    if (j == K - 1) kth = dk[j];
-  const float theta = key_value(static_cast<uint32_t>(kth >> 32));
-  // exact logits of the candidates
-  bool cand[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    cand[i] = lane + 32 * i < E && fu[i] >= theta;
-    unsigned m = __ballot_sync(0xffffffffu, cand[i]);
-    while (m) {
-      const int b = __ffs(m) - 1;
-      m &= m - 1u;
-      const int e = b + 32 * i;
-      const float v = exact_dot(xv, p.router_w + static_cast<size_t>(e) * H, H, lane);
-      if (lane == b) fx[i] = logit_map(p, v, e);
-    }
-  }
-  float gcoef = 1.f;
-  if (p.sh_gate) gcoef = bf16_round(1.f / (1.f + expf(-bf16_round(exact_dot(xv, p.sh_gate, H, lane)))));
-  uint64_t k[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    k[i] = cand[i] ? (static_cast<uint64_t>(order_key(fx[i])) << 32) | static_cast<uint32_t>(~(lane + 32 * i)) : 0ull;
   warp_top8(k);
   int sel_e[8];
   float sel_v[8];
@@ -439,150 +505,190 @@ __global__ void __launch_bounds__(kSelWarps * 32) select_kernel(const __grid_con
     if (p.ids_out) p.ids_out[t * K + lane] = my_e;
     if (p.w_out) p.w_out[t * K + lane] = wb;
   }
-  if (lane == 0) ws_at<float>(p, L.gate)[t] = gcoef;
+  if (lane == 0) ws_at<float>(p, L.gate)[t] = gate_row ? sm.gcoef : 1.f;
 }
 
-// ------------------------------------------------------------------ plan kernel
-// One CTA. Warp w owns pairs [w * per, (w + 1) * per) in pair order; pass 1 counts each expert per
-// warp, a scan over warps and experts gives each (warp, expert) its first position, and pass 2
-// hands out positions in pair order, so the order is the stable sort of the pairs by expert
-// (argsort(ids.flatten(), stable=True)). Tiles: ceil(n_e / 64) per expert, in expert order, then the
-// shared expert's tiles over all T tokens.
-__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const __grid_constant__ Params p) {
-  extern __shared__ int psm[];
+// ------------------------------------------------------------------ dispatch kernel
+// Plan and dispatch in one launch. The dispatch order is the stable sort of the (token, k) pairs
+// by expert (argsort(ids.flatten(), stable=True)): pair i of expert e goes to position
+// off[e] + (pairs of expert e before i). A "pair CTA" owns pairs [a, b): it counts every pair's
+// expert and those before a (one pass over the T * K expert ids, from L2), scans the counts into
+// offsets, ranks its own pairs in order, and writes each pair's position and its token's row split
+// exactly into e4m3 hi + lo rows (x * 2^e, e from the token's absolute maximum). "Shared CTAs"
+// write the shared expert's positions P + t. CTA 0 also writes the tile list (ceil(n_e / 64) tiles
+// per expert in expert order, then the shared expert's tiles), the per-expert offsets and the
+// counts the expert kernels read.
+constexpr int kDispThreads = 256;
+constexpr int kDispWarps = kDispThreads / 32;
+constexpr int kMaxPpc = 1024;  // pairs per CTA (T * K <= 256 * kMaxPpc)
+
+__host__ __device__ inline int pairs_per_cta(int P) {
+  const int ppc = (P + 255) / 256;
+  return ppc < 32 ? 32 : (ppc + 31) / 32 * 32;
+}
+
+// Splits token row t into the hi / lo rows of position pos (one warp).
+__device__ __forceinline__ void split_row(const Params& p, const Layout& L, int pos, int t, int lane) {
+  const int ex = __ldcg(ws_at<const int>(p, L.xexp) + t);
+  const float sc = exp2i(ex);
+  if (lane == 0) ws_at<float>(p, L.pxinv)[pos] = exp2i(-ex);
+  const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
+  uint8_t* hi_row = p.ws + L.pimg + static_cast<size_t>(2 * pos) * p.H;
+  uint8_t* lo_row = hi_row + p.H;
+  constexpr int kC = kMaxH / 16 / 32;  // 16-element chunks per lane at H = 2048
+  uint4 v[kC][2];
+#pragma unroll
+  for (int i = 0; i < kC; ++i) {
+    const int c = lane + 32 * i;
+    if (c < p.H / 16) {
+      v[i][0] = __ldg(src + 2 * c);
+      v[i][1] = __ldg(src + 2 * c + 1);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kC; ++i) {
+    const int c = lane + 32 * i;
+    if (c < p.H / 16) {
+      uint4 hi, lo;
+      split16(v[i], sc, hi, lo);
+      *reinterpret_cast<uint4*>(hi_row + 16 * c) = hi;
+      *reinterpret_cast<uint4*>(lo_row + 16 * c) = lo;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_constant__ Params p) {
+  __shared__ int hist[kMaxRouter], before[kMaxRouter], off[kMaxRouter + 1], tbase[kMaxRouter + 1];
+  __shared__ int spos[kMaxPpc];
   const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
-  const int E = p.E, K = p.K, T = p.T, P = T * K;
-  const bool sh = p.sh_w13 != nullptr;
-  int* wc = psm;            // [32][E]
-  int* cnt = wc + 32 * E;   // [E]
-  int* off = cnt + E;       // [E + 1]
-  int* tb = off + E + 1;    // [E + 1]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < 32 * E; i += kPlanThreads) wc[i] = 0;
+  const int E = p.E, K = p.K, T = p.T, P = T * K;
+  const int ppc = pairs_per_cta(P);
+  const int n_pair_ctas = (P + ppc - 1) / ppc;
   griddep_wait();
   griddep_launch();
-  __syncthreads();
-  const int* pair_e = ws_at<const int>(p, L.pair_e);
-  const int per = (P + 32 * 32 - 1) / (32 * 32) * 32;
-  for (int r = 0; r < per; r += 32) {
-    const int idx = warp * per + r + lane;
-    const int e = idx < P ? __ldcg(pair_e + idx) : -1;
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    if (e >= 0 && lane == __ffs(m) - 1) wc[warp * E + e] += __popc(m);
+  if (static_cast<int>(blockIdx.x) >= n_pair_ctas) {
+    // the shared expert's positions: one warp per token
+    const int t = (blockIdx.x - n_pair_ctas) * kDispWarps + warp;
+    if (p.sh_w13 != nullptr && t < T) {
+      if (lane == 0) ws_at<int>(p, L.pos_tok)[P + t] = t;
+      split_row(p, L, P + t, t, lane);
+    }
+    return;
+  }
+  const int a = blockIdx.x * ppc, b = min(P, a + ppc);
+  for (int e = tid; e < kMaxRouter; e += kDispThreads) {
+    hist[e] = 0;
+    before[e] = 0;
   }
   __syncthreads();
-  for (int e = tid; e < E; e += kPlanThreads) {
-    int run = 0;
-    for (int w = 0; w < 32; ++w) {
-      const int c = wc[w * E + e];
-      wc[w * E + e] = run;
-      run += c;
+  const int* pair_e = ws_at<const int>(p, L.pair_e);
+  for (int i0 = 4 * tid; i0 < P; i0 += 4 * kDispThreads) {
+    int ev[4];
+    if (i0 + 3 < P && (P & 3) == 0) {
+      const int4 v = __ldcg(reinterpret_cast<const int4*>(pair_e + i0));
+      ev[0] = v.x, ev[1] = v.y, ev[2] = v.z, ev[3] = v.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ev[u] = i0 + u < P ? __ldcg(pair_e + i0 + u) : -1;
     }
-    cnt[e] = run;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (ev[u] >= 0) {
+        atomicAdd(&hist[ev[u]], 1);
+        if (i0 + u < a) atomicAdd(&before[ev[u]], 1);
+      }
   }
   __syncthreads();
   if (warp == 0) {
+    // exclusive scans of the counts and of the tile counts (8 experts per lane, in order)
     const int per_l = (E + 31) / 32;
     int s = 0, st = 0;
     for (int j = 0; j < per_l; ++j) {
       const int e = lane * per_l + j;
       if (e < E) {
-        s += cnt[e];
-        st += (cnt[e] + kTileTok - 1) / kTileTok;
+        s += hist[e];
+        st += (hist[e] + kTileTok - 1) / kTileTok;
       }
     }
     int incl = s, inclt = st;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int a = __shfl_up_sync(0xffffffffu, incl, o), b = __shfl_up_sync(0xffffffffu, inclt, o);
+      const int x = __shfl_up_sync(0xffffffffu, incl, o), y = __shfl_up_sync(0xffffffffu, inclt, o);
       if (lane >= o) {
-        incl += a;
-        inclt += b;
+        incl += x;
+        inclt += y;
       }
     }
-    int base = incl - s, tbase = inclt - st;
+    int base = incl - s, tb = inclt - st;
     for (int j = 0; j < per_l; ++j) {
       const int e = lane * per_l + j;
       if (e < E) {
         off[e] = base;
-        tb[e] = tbase;
-        base += cnt[e];
-        tbase += (cnt[e] + kTileTok - 1) / kTileTok;
+        tbase[e] = tb;
+        base += hist[e];
+        tb += (hist[e] + kTileTok - 1) / kTileTok;
       }
     }
     if (lane == 31) {
       off[E] = incl;
-      tb[E] = inclt;
+      tbase[E] = inclt;
+    }
+    __syncwarp();
+    // ranks of this CTA's pairs, in pair order, 32 at a time
+    int* pos_tok = ws_at<int>(p, L.pos_tok);
+    int* inv = ws_at<int>(p, L.inv);
+    for (int i0 = a; i0 < b; i0 += 32) {
+      const int i = i0 + lane;
+      const int e = i < b ? __ldcg(pair_e + i) : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, e);
+      const int rank = e >= 0 ? before[e] + __popc(m & ((1u << lane) - 1u)) : 0;
+      __syncwarp();
+      if (e >= 0 && lane == __ffs(m) - 1) before[e] += __popc(m);
+      __syncwarp();
+      const int pos = e >= 0 ? off[e] + rank : -1;
+      if (i < b) {
+        spos[i - a] = pos;
+        inv[i] = pos;
+        if (pos >= 0) {
+          pos_tok[pos] = i / K;
+          if (p.perm_out) p.perm_out[pos] = i;
+        }
+      }
     }
   }
   __syncthreads();
-  const int nvalid = off[E], nt_routed = tb[E];
-  const int nt_sh = sh ? (T + kTileTok - 1) / kTileTok : 0;
-  int4* tiles = ws_at<int4>(p, L.tiles);
-  for (int e = tid; e < E; e += kPlanThreads) {
-    const int n = cnt[e];
-    for (int j = 0; j * kTileTok < n; ++j) tiles[tb[e] + j] = make_int4(e, off[e] + j * kTileTok, min(kTileTok, n - j * kTileTok), 0);
-  }
-  for (int j = tid; j < nt_sh; j += kPlanThreads) tiles[nt_routed + j] = make_int4(-1, P + j * kTileTok, min(kTileTok, T - j * kTileTok), 0);
-  int* perm = ws_at<int>(p, L.perm);
-  int* pos_tok = ws_at<int>(p, L.pos_tok);
-  int* inv = ws_at<int>(p, L.inv);
-  for (int r = 0; r < per; r += 32) {
-    const int idx = warp * per + r + lane;
-    const int e = idx < P ? __ldcg(pair_e + idx) : -1;
-    const unsigned m = __match_any_sync(0xffffffffu, e);
-    const int rank = e >= 0 ? wc[warp * E + e] + __popc(m & ((1u << lane) - 1u)) : 0;
-    __syncwarp();
-    if (e >= 0 && lane == __ffs(m) - 1) wc[warp * E + e] += __popc(m);
-    __syncwarp();
-    if (e >= 0) {
-      const int pos = off[e] + rank;
-      perm[pos] = idx;
-      pos_tok[pos] = idx / K;
-      inv[idx] = pos;
-      if (p.perm_out) p.perm_out[pos] = idx;
-    } else if (idx < P) {
-      inv[idx] = -1;
+  if (blockIdx.x == 0) {
+    const int nt_routed = tbase[E];
+    const int nt_sh = p.sh_w13 != nullptr ? (T + kTileTok - 1) / kTileTok : 0;
+    int4* tiles = ws_at<int4>(p, L.tiles);
+    for (int e = tid; e < E; e += kDispThreads) {
+      const int n = hist[e];
+      for (int j = 0; j * kTileTok < n; ++j)
+        tiles[tbase[e] + j] = make_int4(e, off[e] + j * kTileTok, min(kTileTok, n - j * kTileTok), 0);
+    }
+    for (int j = tid; j < nt_sh; j += kDispThreads)
+      tiles[nt_routed + j] = make_int4(-1, P + j * kTileTok, min(kTileTok, T - j * kTileTok), 0);
+    if (p.offsets_out)
+      for (int e = tid; e <= E; e += kDispThreads) p.offsets_out[e] = off[e];
+    if (tid == 0) {
+      uint32_t* c = ws_at<uint32_t>(p, L.ctrl);
+      c[C_NTILES] = static_cast<uint32_t>(nt_routed + nt_sh);
+      c[C_NVALID] = static_cast<uint32_t>(off[E]);
     }
   }
-  for (int t = tid; t < T; t += kPlanThreads) pos_tok[P + t] = t;
-  if (p.offsets_out)
-    for (int e = tid; e <= E; e += kPlanThreads) p.offsets_out[e] = off[e];
-  if (tid == 0) {
-    uint32_t* c = ws_at<uint32_t>(p, L.ctrl);
-    c[C_NTILES] = static_cast<uint32_t>(nt_routed + nt_sh);
-    c[C_NVALID] = static_cast<uint32_t>(nvalid);
-  }
-}
-
-// ------------------------------------------------------------------ dispatch kernel
-// One warp per position: the token's row x * 2^e (e from the token's absolute maximum) split
-// exactly into e4m3 hi and lo rows of the permuted activation image.
-__global__ void __launch_bounds__(kDispatchWarps * 32) dispatch_kernel(const __grid_constant__ Params p) {
-  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int pos = blockIdx.x * kDispatchWarps + warp;
-  const int P = p.T * p.K;
-  griddep_wait();
-  griddep_launch();
-  const int nvalid = static_cast<int>(__ldcg(ws_at<const uint32_t>(p, L.ctrl) + C_NVALID));
-  if (!(pos < nvalid || (p.sh_w13 != nullptr && pos >= P && pos < P + p.T))) return;
-  const int t = __ldcg(ws_at<const int>(p, L.pos_tok) + pos);
-  const float sc = exp2i(__ldcg(ws_at<const int>(p, L.xexp) + t));
-  const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
-  uint8_t* hi_row = p.ws + L.pimg + static_cast<size_t>(2 * pos) * p.H;
-  uint8_t* lo_row = hi_row + p.H;
-  for (int c = lane; c < p.H / 16; c += 32) {
-    const uint4 v[2] = {__ldg(src + 2 * c), __ldg(src + 2 * c + 1)};
-    uint4 hi, lo;
-    split16(v, sc, hi, lo);
-    *reinterpret_cast<uint4*>(hi_row + 16 * c) = hi;
-    *reinterpret_cast<uint4*>(lo_row + 16 * c) = lo;
+  // the permuted activation rows of this CTA's pairs
+  for (int j = warp; j < b - a; j += kDispWarps) {
+    const int pos = spos[j];
+    if (pos >= 0) split_row(p, L, pos, (a + j) / K, lane);
   }
 }
 
 // ------------------------------------------------------------------ up / down kernels
+constexpr int kMaxItems = 64;  // items per CTA whose descriptors are staged in shared memory
+
 struct Aux {
+  int4 items[kMaxItems];  // (expert or -1, first position, tokens, row block) of the CTA's items
   uint64_t full[8], empty[8];
   uint64_t acc_full[4], acc_empty[4];
   uint64_t mma_done;
@@ -594,6 +700,15 @@ struct Aux {
 // Activation box of a tile of n tokens: 2n rows rounded up to 16, 32, 64 or 128 (the MMA's N).
 __device__ __forceinline__ int box_index(int n) { return n <= 8 ? 0 : n <= 16 ? 1 : n <= 32 ? 2 : 3; }
 
+// Item k of this CTA (k-th of blockIdx.x, blockIdx.x + gridDim.x, ...): staged in shared memory at
+// kernel start, read from the tile list beyond kMaxItems.
+__device__ __forceinline__ int4 item_desc(const Aux& aux, const int4* tiles, int nrb, int k) {
+  if (k < kMaxItems) return aux.items[k];
+  const int idx = blockIdx.x + k * gridDim.x;
+  const int4 tl = __ldcg(tiles + idx / nrb);
+  return make_int4(tl.x, tl.y, tl.z, idx % nrb);
+}
+
 template <bool DOWN>
 __global__ void __launch_bounds__(kThreads, 1)
     expert_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map_w,
@@ -602,23 +717,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const __grid_constant__ CUtensorMap map_b3) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  constexpr int kStages = DOWN ? kDownStages : kUpStages;
-  constexpr int kStage = DOWN ? kDownStage : kUpStage;
-  constexpr int kBOff = DOWN ? kSlab : 2 * kSlab;  // activation slab inside a stage
-  constexpr int kNacc = DOWN ? kDownAcc : kUpAcc;
-  constexpr uint32_t kAccCols = DOWN ? 128 : 256;
+  constexpr int kBOff = 2 * kSlab;  // activation slab inside a stage
+  constexpr uint32_t kAccCols = 256;
   Aux& aux = *reinterpret_cast<Aux*>(smem + kStages * kStage);
   const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nrb = (DOWN ? p.H : p.I) / kRows;  // weight row blocks per tile
+  // items: up 128 gate rows + the matching 128 up rows; down 256 output rows (two 128-row halves)
+  const int nrb = DOWN ? p.H / (2 * kRows) : p.I / kRows;
   const int nkb = (DOWN ? p.I : p.H) / 128;    // k slabs per item
-  // the plan kernel ran at least two launches back, so its tiles are complete
+  // the tile list is written by the dispatch kernel: the up kernel (its successor) waits for it,
+  // the down kernel (two launches later) finds it complete
+  if (!DOWN) griddep_wait();
   const int ntiles = static_cast<int>(__ldcg(ws_at<const uint32_t>(p, L.ctrl) + C_NTILES));
   const int n_items = ntiles * nrb;
   const int my_items = n_items > static_cast<int>(blockIdx.x) ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int4* tiles = ws_at<const int4>(p, L.tiles);
   volatile int* abort = &aux.abort;
 
+  if (tid < my_items && tid < kMaxItems) {
+    const int idx = blockIdx.x + tid * gridDim.x;
+    const int4 tl = __ldcg(tiles + idx / nrb);
+    aux.items[tid] = make_int4(tl.x, tl.y, tl.z, idx % nrb);
+  }
   if (tid == 0) {
     tc::prefetch_map(&map_w);
     if (p.sh_w13) tc::prefetch_map(&map_sh);
@@ -644,44 +764,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================================================ TMA producer (lane 0)
     if (lane == 0) {
       const int total = my_items * nkb;
-      auto stage_ptr = [&](int s) { return smem + (s % kStages) * kStage; };
-      auto item_tile = [&](int s, int& rb, int& kb) {
-        const int k = s / nkb;
-        kb = s % nkb;
-        const int idx = blockIdx.x + k * gridDim.x;
-        rb = idx % nrb;
-        return __ldcg(tiles + idx / nrb);
-      };
-      auto issue_a = [&](int s) {
-        int rb, kb;
-        const int4 tl = item_tile(s, rb, kb);
-        const CUtensorMap* map = tl.x < 0 ? &map_sh : &map_w;
-        const int plane = tl.x < 0 ? 0 : tl.x;
-        uint8_t* dst = stage_ptr(s);
+      auto issue_a = [&](int s, const int4& it, int kb) {
+        const CUtensorMap* map = it.x < 0 ? &map_sh : &map_w;
+        const int plane = it.x < 0 ? 0 : it.x;
+        uint8_t* dst = smem + (s % kStages) * kStage;
         uint64_t* bar = &aux.full[s % kStages];
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kBOff + (16 << box_index(tl.z)) * 128));
-        tc::tma_load_3d(dst, map, kb * 128, kRows * rb, plane, bar);
-        if (!DOWN) tc::tma_load_3d(dst + kSlab, map, kb * 128, p.I + kRows * rb, plane, bar);
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kBOff + (16 << box_index(it.z)) * 128));
+        const int row0 = DOWN ? 2 * kRows * it.w : kRows * it.w;
+        const int row1 = DOWN ? row0 + kRows : p.I + kRows * it.w;
+        tc::tma_load_3d(dst, map, kb * 128, row0, plane, bar);
+        tc::tma_load_3d(dst + kSlab, map, kb * 128, row1, plane, bar);
       };
-      auto issue_b = [&](int s) {
-        int rb, kb;
-        const int4 tl = item_tile(s, rb, kb);
-        const int bi = box_index(tl.z);
+      auto issue_b = [&](int s, const int4& it, int kb) {
+        const int bi = box_index(it.z);
         const CUtensorMap* map = bi == 0 ? &map_b0 : bi == 1 ? &map_b1 : bi == 2 ? &map_b2 : &map_b3;
-        tc::tma_load_3d(stage_ptr(s) + kBOff, map, kb * 128, 2 * tl.y, 0, &aux.full[s % kStages]);
+        tc::tma_load_3d(smem + (s % kStages) * kStage + kBOff, map, kb * 128, 2 * it.y, 0, &aux.full[s % kStages]);
       };
       // the weight slabs of the first ring before the wait; activation slabs (from the preceding
       // kernel) after it
       const int first = min(total, kStages);
-      for (int s = 0; s < first; ++s) issue_a(s);
+      for (int s = 0; s < first; ++s) issue_a(s, item_desc(aux, tiles, nrb, s / nkb), s % nkb);
       griddep_wait();
       griddep_launch();
-      for (int s = 0; s < first; ++s) issue_b(s);
+      for (int s = 0; s < first; ++s) issue_b(s, item_desc(aux, tiles, nrb, s / nkb), s % nkb);
+      int k = first / nkb, kb = first % nkb;
+      int4 it = item_desc(aux, tiles, nrb, k < my_items ? k : 0);
       for (int s = first; s < total; ++s) {
-        const int st = s % kStages;
-        wait_or_abort(p, &aux.empty[st], ((s / kStages) & 1) ^ 1u, abort);
-        issue_a(s);
-        issue_b(s);
+        wait_or_abort(p, &aux.empty[s % kStages], ((s / kStages) & 1) ^ 1u, abort);
+        issue_a(s, it, kb);
+        issue_b(s, it, kb);
+        if (++kb == nkb) {
+          kb = 0;
+          if (++k < my_items) it = item_desc(aux, tiles, nrb, k);
+        }
       }
       // nothing may still be copying into shared memory when the CTA exits (bounded waits, also
       // after an abort)
@@ -693,9 +808,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int s = 0, use = 0;
       for (int k = 0; k < my_items; ++k) {
-        const int idx = blockIdx.x + k * gridDim.x;
-        const int4 tl = __ldcg(tiles + idx / nrb);
-        const uint32_t idesc = tc::idesc_e4m3(kRows, 16 << box_index(tl.z));
+        const int4 it = item_desc(aux, tiles, nrb, k);
+        const uint32_t idesc = tc::idesc_e4m3(kRows, 16 << box_index(it.z));
         for (int kb = 0; kb < nkb; ++kb, ++s, ++use) {
           const int ab = use % kNacc;
           wait_or_abort(p, &aux.acc_empty[ab], ((use / kNacc) & 1) ^ 1u, abort);
@@ -707,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k4 = 0; k4 < 4; ++k4) {
             tc::mma_f8(d, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
-            if (!DOWN) tc::mma_f8(d + 128, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+            tc::mma_f8(d + 128, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
           }
           tc::mma_commit(&aux.empty[s % kStages]);
           tc::mma_commit(&aux.acc_full[ab]);
@@ -722,91 +836,171 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3, hf = (warp - 2) >> 2;
     const int r = 32 * q + lane;
     if (DOWN) griddep_wait();  // the h blocks' scales come from the up kernel
-    int use = 0;
-    for (int k = 0; k < my_items; ++k) {
-      const int idx = blockIdx.x + k * gridDim.x;
-      const int4 tl = __ldcg(tiles + idx / nrb);
-      const int rb = idx % nrb;
-      const int nh = min(max(tl.z - 32 * hf, 0), 32);  // this warp's tokens of the tile
-      const int pbase = tl.y + 32 * hf;
-      const bool shared_tile = tl.x < 0;
+    // per-item token data, fetched one item ahead: up 2^-e of each token's x split, down the
+    // token's 2^-e of each 128-block of h
+    auto token_data = [&](const int4& it, float (&v)[kMaxI / 128]) {
+      const int nh = min(max(it.z - 32 * hf, 0), 32);
+      const int pos = it.y + 32 * hf + lane;
+#pragma unroll
+      for (int kb = 0; kb < kMaxI / 128; ++kb) v[kb] = 0.f;
+      if (lane < nh) {
+        if (!DOWN) {
+          v[0] = __ldcg(ws_at<const float>(p, L.pxinv) + pos);
+        } else {
+#pragma unroll
+          for (int kb = 0; kb < kMaxI / 128; ++kb)
+            if (kb < nkb) v[kb] = __ldcg(ws_at<const float>(p, L.hinv) + static_cast<size_t>(pos) * nkb + kb);
+        }
+      }
+    };
+    auto scale_row = [&](const int4& it, bool second) -> const float* {
+      // block scales of this thread's weight row in the item's first or second 128-row half:
+      // [rows / srows][nkb] per expert
+      const bool shared_tile = it.x < 0;
       const int srows = shared_tile ? p.sh_srows : p.srows;
+      if (!DOWN) {
+        const float* s13 = shared_tile ? p.sh_s13 : p.s13 + static_cast<size_t>(it.x) * p.s13_stride;
+        const int row = (second ? p.I : 0) + kRows * it.w + r;
+        return s13 + static_cast<size_t>(row / srows) * nkb;
+      }
+      const float* s2 = shared_tile ? p.sh_s2 : p.s2 + static_cast<size_t>(it.x) * p.s2_stride;
+      return s2 + static_cast<size_t>((2 * kRows * it.w + (second ? kRows : 0) + r) / srows) * nkb;
+    };
+    int use = 0;
+    int4 it_next = my_items > 0 ? item_desc(aux, tiles, nrb, 0) : make_int4(0, 0, 0, 0);
+    float td_next[kMaxI / 128];
+    float sg_next = 0.f, su_next = 0.f;  // the next item's first-slab scales
+    if (my_items > 0) {
+      token_data(it_next, td_next);
+      sg_next = __ldg(scale_row(it_next, false));
+      su_next = __ldg(scale_row(it_next, true));
+    }
+    for (int k = 0; k < my_items; ++k) {
+      const int4 it = it_next;
+      float td[kMaxI / 128];
+#pragma unroll
+      for (int i = 0; i < kMaxI / 128; ++i) td[i] = td_next[i];
+      float sg = sg_next, su = su_next;
+      if (k + 1 < my_items) {
+        it_next = item_desc(aux, tiles, nrb, k + 1);
+        token_data(it_next, td_next);
+        sg_next = __ldg(scale_row(it_next, false));
+        su_next = __ldg(scale_row(it_next, true));
+      }
+      const int nh = min(max(it.z - 32 * hf, 0), 32);  // this warp's tokens of the tile
+      const int pbase = it.y + 32 * hf;
+      const bool shared_tile = it.x < 0;
+      const float* sgp = scale_row(it, false);
+      const float* sup = scale_row(it, true);
       float a0[32], a1[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) a0[j] = a1[j] = 0.f;
-      if (!DOWN) {
-        const float* s13 = shared_tile ? p.sh_s13 : p.s13 + static_cast<size_t>(tl.x) * p.s13_stride;
-        float sg[kMaxH / 128], su[kMaxH / 128];
-        const int rg = kRows * rb + r, ru = p.I + kRows * rb + r;
-#pragma unroll
-        for (int kb = 0; kb < kMaxH / 128; ++kb) {
-          sg[kb] = kb < nkb ? __ldg(s13 + static_cast<size_t>(rg / srows) * nkb + kb) : 0.f;
-          su[kb] = kb < nkb ? __ldg(s13 + static_cast<size_t>(ru / srows) * nkb + kb) : 0.f;
-        }
-        float xi = 0.f;
-        if (lane < nh) xi = exp2i(-__ldcg(ws_at<const int>(p, L.xexp) + __ldcg(ws_at<const int>(p, L.pos_tok) + pbase + lane)));
-#pragma unroll
-        for (int kb = 0; kb < kMaxH / 128; ++kb) {
-          if (kb < nkb) {
-            const int ab = use % kNacc;
-            bool ready = true;
-            if (lane == 0) ready = wait_or_abort(p, &aux.acc_full[ab], (use / kNacc) & 1, abort);
-            ready = __shfl_sync(0xffffffffu, ready, 0);
-            ++use;
-            tc::fence_after_sync();
-            if (nh > 0 && ready) {
-              const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
-              float v0[32], v1[32];
-              tc::tmem_ld32(ta, v0);
-              tc::tmem_ld32(ta + 32, v1);
-              tc::tmem_wait_ld();
+      // the up kernel's 16 slabs stay a rolled loop: unrolled, its code would push the item tail
+      // out of the instruction cache on every item
+#pragma unroll(DOWN ? kMaxI / 128 : 1)
+      for (int kb = 0; kb < (DOWN ? kMaxI / 128 : nkb); ++kb) {
+        if (kb < nkb) {
+          // the next slab's scales are requested before this slab's accumulator is read
+          float sg_n = 0.f, su_n = 0.f;
+          if (kb + 1 < nkb) {
+            sg_n = __ldg(sgp + kb + 1);
+            su_n = __ldg(sup + kb + 1);
+          }
+          const int ab = use % kNacc;
+          bool ready = true;
+          if (lane == 0) ready = wait_or_abort(p, &aux.acc_full[ab], (use / kNacc) & 1, abort);
+          ready = __shfl_sync(0xffffffffu, ready, 0);
+          ++use;
+          tc::fence_after_sync();
+          if (nh > 0 && ready) {
+            const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
+            float v0[32], v1[32];
+            tc::tmem_ld32(ta, v0);
+            tc::tmem_ld32(ta + 32, v1);
+            tc::tmem_wait_ld();
+            if (!DOWN) {
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                a0[j] = fmaf(sg[kb], v0[2 * j] + v0[2 * j + 1], a0[j]);
-                a0[16 + j] = fmaf(sg[kb], v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
+                a0[j] = fmaf(sg, v0[2 * j] + v0[2 * j + 1], a0[j]);
+                a0[16 + j] = fmaf(sg, v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
               }
               tc::tmem_ld32(ta + 128, v0);
               tc::tmem_ld32(ta + 160, v1);
               tc::tmem_wait_ld();
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
-                a1[j] = fmaf(su[kb], v0[2 * j] + v0[2 * j + 1], a1[j]);
-                a1[16 + j] = fmaf(su[kb], v1[2 * j] + v1[2 * j + 1], a1[16 + j]);
+                a1[j] = fmaf(su, v0[2 * j] + v0[2 * j + 1], a1[j]);
+                a1[16 + j] = fmaf(su, v1[2 * j] + v1[2 * j + 1], a1[16 + j]);
+              }
+            } else {
+              float hk = td[0];
+#pragma unroll
+              for (int i = 1; i < kMaxI / 128; ++i)
+                if (kb == i) hk = td[i];
+              float hj[32];  // 2^-e of each token's h block
+#pragma unroll
+              for (int j = 0; j < 32; ++j) hj[j] = __shfl_sync(0xffffffffu, hk, j);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                a0[j] = fmaf(sg * hj[j], v0[2 * j] + v0[2 * j + 1], a0[j]);
+                a0[16 + j] = fmaf(sg * hj[16 + j], v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
+              }
+              tc::tmem_ld32(ta + 128, v0);
+              tc::tmem_ld32(ta + 160, v1);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                a1[j] = fmaf(su * hj[j], v0[2 * j] + v0[2 * j + 1], a1[j]);
+                a1[16 + j] = fmaf(su * hj[16 + j], v1[2 * j] + v1[2 * j + 1], a1[16 + j]);
               }
             }
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&aux.acc_empty[ab]);
           }
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&aux.acc_empty[ab]);
+          sg = sg_n;
+          su = su_n;
         }
+      }
+      if (!DOWN) {
         // SwiGLU, h rounded to bf16 (the reference's activation dtype; the shared expert is a chain
         // of bf16 modules), then the per-(token, 128-block) absolute maxima across the 4 quarters
         const int par = k & 1;
+        const float xi = td[0];
+        // branch-free over the 32 tokens: the shared expert's extra bf16 roundings are selects, the
+        // tokens past the tile's end are zeroed
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float xj = __shfl_sync(0xffffffffu, xi, j);
-          float h = 0.f;
-          if (j < nh) {
-            float g = a0[j] * xj, u = a1[j] * xj;
-            if (shared_tile) {
-              g = bf16_round(g);
-              u = bf16_round(u);
-              h = bf16_round(bf16_round(g * __frcp_rn(1.f + __expf(-g))) * u);
-            } else {
-              h = bf16_round(g * __frcp_rn(1.f + __expf(-g)) * u);
-            }
-          }
+          float g = a0[j] * xj, u = a1[j] * xj;
+          g = shared_tile ? bf16_round(g) : g;
+          u = shared_tile ? bf16_round(u) : u;
+          float sl = __fdividef(g, 1.f + __expf(-g));
+          sl = shared_tile ? bf16_round(sl) : sl;
+          const float h = j < nh ? bf16_round(sl * u) : 0.f;
           a0[j] = h;
-          const uint32_t am = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h)));
-          if (lane == j) aux.amax[par][hf][q][j] = __uint_as_float(am);
+          a1[j] = fabsf(h);
         }
+        // transposing max over the warp's 32 rows: after the halving steps lane j holds the
+        // maximum of token j (31 shuffles for all 32 tokens)
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+          const bool upper = (lane & d) != 0;
+#pragma unroll
+          for (int i = 0; i < d; ++i) {
+            const float send = upper ? a1[i] : a1[i + d];
+            const float keep = upper ? a1[i + d] : a1[i];
+            a1[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, d));
+          }
+        }
+        aux.amax[par][hf][q][lane] = a1[0];
         named_bar(kBarEpi, kEpiThreads);
         float e2[32];
         const int e_mine = split_exponent(fmaxf(fmaxf(aux.amax[par][hf][0][lane], aux.amax[par][hf][1][lane]),
                                                 fmaxf(aux.amax[par][hf][2][lane], aux.amax[par][hf][3][lane])));
 #pragma unroll
         for (int j = 0; j < 32; ++j) e2[j] = exp2i(__shfl_sync(0xffffffffu, e_mine, j));
-        uint8_t* himg = p.ws + L.himg + static_cast<size_t>(2 * pbase) * p.I + kRows * rb + r;
+        uint8_t* himg = p.ws + L.himg + static_cast<size_t>(2 * pbase) * p.I + kRows * it.w + r;
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           if (j < nh) {
@@ -820,48 +1014,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (q == 0 && lane < nh) ws_at<float>(p, L.hinv)[static_cast<size_t>(pbase + lane) * (p.I / 128) + rb] = exp2i(-e_mine);
+        if (q == 0 && lane < nh)
+          ws_at<float>(p, L.hinv)[static_cast<size_t>(pbase + lane) * (p.I / 128) + it.w] = exp2i(-e_mine);
       } else {
-        const float* s2 = shared_tile ? p.sh_s2 : p.s2 + static_cast<size_t>(tl.x) * p.s2_stride;
-        float sd[kMaxI / 128], hv[kMaxI / 128];
-        const int ro = kRows * rb + r;
-#pragma unroll
-        for (int kb = 0; kb < kMaxI / 128; ++kb) {
-          sd[kb] = kb < nkb ? __ldg(s2 + static_cast<size_t>(ro / srows) * nkb + kb) : 0.f;
-          hv[kb] = kb < nkb && lane < nh ? __ldcg(ws_at<const float>(p, L.hinv) + static_cast<size_t>(pbase + lane) * nkb + kb) : 0.f;
-        }
-#pragma unroll
-        for (int kb = 0; kb < kMaxI / 128; ++kb) {
-          if (kb < nkb) {
-            const int ab = use % kNacc;
-            bool ready = true;
-            if (lane == 0) ready = wait_or_abort(p, &aux.acc_full[ab], (use / kNacc) & 1, abort);
-            ready = __shfl_sync(0xffffffffu, ready, 0);
-            ++use;
-            tc::fence_after_sync();
-            if (nh > 0 && ready) {
-              const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
-              float v0[32], v1[32];
-              tc::tmem_ld32(ta, v0);
-              tc::tmem_ld32(ta + 32, v1);
-              tc::tmem_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const float c0 = sd[kb] * __shfl_sync(0xffffffffu, hv[kb], j);
-                const float c1 = sd[kb] * __shfl_sync(0xffffffffu, hv[kb], 16 + j);
-                a0[j] = fmaf(c0, v0[2 * j] + v0[2 * j + 1], a0[j]);
-                a0[16 + j] = fmaf(c1, v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
-              }
-            }
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&aux.acc_empty[ab]);
-          }
-        }
-        float* out = ws_at<float>(p, L.outp) + static_cast<size_t>(pbase) * p.H + kRows * rb + r;
+        float* out = ws_at<float>(p, L.outp) + static_cast<size_t>(pbase) * p.H + 2 * kRows * it.w + r;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j < nh) __stcg(out + static_cast<size_t>(j) * p.H, a0[j]);
+          if (j < nh) {
+            __stcg(out + static_cast<size_t>(j) * p.H, a0[j]);
+            __stcg(out + static_cast<size_t>(j) * p.H + kRows, a1[j]);
+          }
       }
     }
   }
@@ -956,8 +1118,8 @@ int pf_launch(void (*kernel)(KArgs...), dim3 grid, int block, size_t smem, cudaS
   return 0;
 }
 
-constexpr size_t kExpertSmem(bool down) {
-  return static_cast<size_t>(down ? pf::kDownStages * pf::kDownStage : pf::kUpStages * pf::kUpStage) + 1024 +
+constexpr size_t kExpertSmem(bool) {
+  return static_cast<size_t>(pf::kStages * pf::kStage) + 1024 +
          ((sizeof(pf::Aux) + 127) / 128) * 128;
 }
 
@@ -974,7 +1136,6 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream) {
   static bool attrs_set = false;
   if (!attrs_set) {
     cudaFuncSetAttribute(pf::logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem);
-    cudaFuncSetAttribute(pf::plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     cudaFuncSetAttribute(pf::expert_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(kExpertSmem(false)));
     cudaFuncSetAttribute(pf::expert_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1009,14 +1170,12 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream) {
     if (pf_launch(pf::logits_kernel, g, pf::kLgThreads, pf::kLgSmem, stream, "prefill logits", p, mr, mx)) return 2;
     ++n;
   }
-  if (pf_launch(pf::select_kernel, dim3((p.T + pf::kSelWarps - 1) / pf::kSelWarps), pf::kSelWarps * 32, 0, stream,
-                "prefill select", p))
+  if (pf_launch(pf::select_kernel, dim3(p.T), pf::kSelThreads, 0, stream, "prefill select", p))
     return 2;
-  const size_t plan_smem = static_cast<size_t>(32 * E + E + 2 * (E + 1)) * 4;
-  if (pf_launch(pf::plan_kernel, dim3(1), pf::kPlanThreads, plan_smem, stream, "prefill plan", p)) return 2;
-  if (pf_launch(pf::dispatch_kernel, dim3((L.npos + pf::kDispatchWarps - 1) / pf::kDispatchWarps),
-                pf::kDispatchWarps * 32, 0, stream, "prefill dispatch", p))
-    return 2;
+  const int P = p.T * p.K;
+  const int disp_ctas = (P + pf::pairs_per_cta(P) - 1) / pf::pairs_per_cta(P) +
+                        (p.sh_w13 ? (p.T + pf::kDispWarps - 1) / pf::kDispWarps : 0);
+  if (pf_launch(pf::dispatch_kernel, dim3(disp_ctas), pf::kDispThreads, 0, stream, "prefill dispatch", p)) return 2;
   if (pf_launch(pf::expert_kernel<false>, dim3(sms), pf::kThreads, kExpertSmem(false), stream, "prefill up", p, m13,
                 msh13, mb_up[0], mb_up[1], mb_up[2], mb_up[3]))
     return 2;
@@ -1027,7 +1186,7 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream) {
   if (pf_launch(pf::combine_kernel, dim3((c_threads + pf::kCombineThreads - 1) / pf::kCombineThreads),
                 pf::kCombineThreads, 0, stream, "prefill combine", p))
     return 2;
-  note_launches(n + 6);
+  note_launches(n + 5);
   return 0;
 }
 
@@ -1045,8 +1204,7 @@ int launch_route(const pf::Params& p, cudaStream_t stream) {
     return 2;
   const dim3 g((p.E + pf::kRows - 1) / pf::kRows, (p.T + pf::kLgTok - 1) / pf::kLgTok, L.ks);
   if (pf_launch(pf::logits_kernel, g, pf::kLgThreads, pf::kLgSmem, stream, "route logits", p, mr, mx)) return 2;
-  if (pf_launch(pf::select_kernel, dim3((p.T + pf::kSelWarps - 1) / pf::kSelWarps), pf::kSelWarps * 32, 0, stream,
-                "route select", p))
+  if (pf_launch(pf::select_kernel, dim3(p.T), pf::kSelThreads, 0, stream, "route select", p))
     return 2;
   note_launches(2);
   return 0;
@@ -1062,8 +1220,9 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int check_prefill(int T, int H, int I, int E, int top_k, const void* x, const void* w13, int64_t w13_stride,
                   const float* s13, const void* w2, int64_t w2_stride, const float* s2, int srows, const void* y,
                   const void* ws, size_t ws_bytes) {
-  if (T < 1) return dm3::set_error("T must be >= 1"), 1;
-  if (H < 128 || H % 128 || H > dm3::kMaxH) return dm3::set_error("H must be a multiple of 128 in [128, 2048]"), 1;
+  if (T < 1 || static_cast<int64_t>(T) * top_k > 256 * dm3::pf::kMaxPpc)
+    return dm3::set_error("T * top_k must be in [1, 262144]"), 1;
+  if (H < 256 || H % 256 || H > dm3::kMaxH) return dm3::set_error("H must be a multiple of 256 in [256, 2048]"), 1;
   if (I < 128 || I % 128 || I > dm3::kMaxI) return dm3::set_error("I must be a multiple of 128 in [128, 512]"), 1;
   if (top_k < 1 || top_k > dm3::kMaxTopK) return dm3::set_error("top_k must be in [1, 8]"), 1;
   if (E < top_k || E > dm3::kMaxRouter) return dm3::set_error("the expert count must be in [top_k, 256]"), 1;

@@ -180,7 +180,7 @@ size_t dm3_moe_prefill_workspace_bytes(int T, int H, int I, int n_experts, int t
  *   offsets_out  optional int64 [n_router + 1]: first dispatch position of each expert
  * Router logits are those of exact sums rounded once (fp32, then bf16 for logits_bf16), so the
  * chosen experts match an exact reference; ties go to the lower expert index.
- * 1 <= T, H % 128 == 0, H <= 2048, I % 128 == 0, I <= 512, top_k <= n_router <= 256, top_k <= 8.
+ * 1 <= T, H % 256 == 0, H <= 2048, I % 128 == 0, I <= 512, top_k <= n_router <= 256, top_k <= 8.
  */
 int dm3_moe_prefill(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
                     int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride, const float* s13,
