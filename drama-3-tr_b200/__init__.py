@@ -6,7 +6,7 @@ signatures of the reference engine: `fp8_moe_forward`, `Speaker`, `speaker_forwa
 (see drama3_b200.py at the repository root; the directory name has hyphens).
 """
 
-from . import _lib, ops  # noqa: F401
+from . import _lib, ep, ops  # noqa: F401
 from .fp8_linear import BLOCK, FP8Linear, convert, dequantize, quantize  # noqa: F401
 from .fp8_moe import fp8_moe_forward  # noqa: F401
 from .speaker import (  # noqa: F401

@@ -41,6 +41,18 @@ SIGNATURES = {
                              _p, _sz, _p]),
     "dm3_route_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "dm3_route": (_i, [_p, _i, _i, _p, _i, _i, _i, _p, _p, _p, _p, _sz, _p]),
+    "dm3_ep_arena_bytes": (_sz, [_i, _i, _i, _i]),
+    "dm3_ep_alloc": (_i, [_sz, ctypes.POINTER(ctypes.c_void_p)]),
+    "dm3_ep_free": (_i, [_p]),
+    "dm3_ep_ipc_handle": (_i, [_p, _p]),
+    "dm3_ep_ipc_open": (_i, [_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "dm3_ep_ipc_close": (_i, [_p]),
+    "dm3_moe_prefill_ep_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
+    "dm3_moe_prefill_ep": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p,
+                                _p, _p, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
+    "dm3_ep_dispatch": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
+    "dm3_ep_combine": (_i, [_p, _i, _i, _i, _p, _i, _i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p, _p, _p,
+                            _i, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
     "dm3_last_launch_count": (_i, []),
 }
 

@@ -1,7 +1,7 @@
 // Shared device helpers for the drama-3 MoE / block-FP8 kernels (sm_100a only).
 //
 // Everything here is thin inline PTX: mbarrier + cp.async.bulk staging (TMA bulk copies
-// without multicast), gpu-scope acquire/release flags with time-bounded spins, the FP8
+// into the issuing CTA only), gpu-scope acquire/release flags with time-bounded spins, the FP8
 // mma.sync tile used for the skinny (<= 4 row) products, and the exact bf16 -> e4m3 hi/lo
 // split that lets a bf16 activation be multiplied against raw e4m3 weights on the FP8 pipe.
 #pragma once

@@ -108,7 +108,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // ---------------------------------------------------------------- TMA
-// 3-D tiled copy global -> shared (no multicast); completes transaction bytes on the mbarrier.
+// 3-D tiled copy global -> this CTA's shared memory; completes transaction bytes on the mbarrier.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "

@@ -30,6 +30,8 @@
 // barrier is left without its arrivals.
 #include <cfloat>
 #include <cmath>
+#include <cstdint>
+#include <cstring>
 #include <string>
 #include <utility>
 
@@ -62,6 +64,8 @@ constexpr int kBarEpi = 1;                   // named barrier of the up epilogue
 // control words; the status word sits where the decode workspace keeps it, so one reader serves both
 enum : int { C_STATUS = 4, C_NTILES = 8, C_NVALID = 9, C_WORDS = 16 };
 
+constexpr int kMaxRanks = 8;
+
 struct Params {
   int T, H, I, E, K;  // tokens, hidden, intermediate, routed experts (router width), top-k
   int mode;           // 0: routing given (ids / rw), 1: router
@@ -93,6 +97,11 @@ struct Params {
   int64_t* perm_out;
   int64_t* offsets_out;
   uint8_t* ws;
+  // expert parallel (world > 1): this rank routes its own T tokens over all E experts and owns the
+  // el experts [rank * el, (rank + 1) * el), whose weights w13 / w2 hold; ep_arena[r] is rank r's
+  // arena mapped in this process (ep_arena[rank] its own), ep_tl the token capacity of every rank
+  int world, rank, ep_tl, ep_el;
+  uint8_t* ep_arena[kMaxRanks];
 };
 
 // ------------------------------------------------------------------ workspace layout
@@ -101,17 +110,20 @@ struct Params {
 struct Layout {
   size_t ctrl, lpart, wnorm, pair_e, pair_w, gate, xexp, pos_tok, pxinv, perm, inv, tiles, pimg, himg, hinv, outp, total;
   int ks, max_tiles, npos;
+  int cap;  // routed positions [0, cap); the shared expert's positions are cap + t
 };
 
 __host__ __device__ inline size_t aup(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline Layout layout(int T, int H, int I, int E, int K) {
+// cap: routed positions; T * K on one GPU, world * (token capacity per rank) * K under expert
+// parallelism (the pairs every rank may send here).
+__host__ __device__ inline Layout layout(int T, int H, int I, int E, int K, int cap = -1) {
   Layout L;
   const size_t P = static_cast<size_t>(T) * K;
+  L.cap = cap < 0 ? static_cast<int>(P) : cap;
   L.ks = (H + kLgK - 1) / kLgK;
-  L.npos = static_cast<int>(P) + T;
-  L.max_tiles = static_cast<int>((P + kTileTok - 1) / kTileTok) + (E < static_cast<int>(P) ? E : static_cast<int>(P)) +
-                (T + kTileTok - 1) / kTileTok + 1;
+  L.npos = L.cap + T;
+  L.max_tiles = (L.cap + kTileTok - 1) / kTileTok + (E < L.cap ? E : L.cap) + (T + kTileTok - 1) / kTileTok + 1;
   size_t o = 0;
   L.ctrl = o;
   o += C_WORDS * 4;
@@ -149,6 +161,66 @@ __host__ __device__ inline Layout layout(int T, int H, int I, int E, int K) {
   return L;
 }
 
+__host__ __device__ inline Layout layout_of(const Params& p) {
+  return layout(p.T, p.H, p.I, p.E, p.K, p.world > 1 ? p.world * p.ep_tl * p.K : -1);
+}
+
+// ------------------------------------------------------------------ expert-parallel arena
+// Every rank holds one arena, mapped by all ranks (CUDA IPC over NVLink):
+//   ctrl     [16] u32: the call epoch, CTA counters
+//   rflag    [world] u32, rcount [world] u32: written by source rank s after its pairs for this
+//            rank have landed in stage[s] (count first, then the epoch with a system-scope release)
+//   retflag  [world] u32: written by destination rank d after every output row for this rank's
+//            pairs has landed in ret
+//   rmeta    [world][tl * K] int2: (local expert << 20 | source pair index, x split exponent)
+//   stage    [world][tl * K][2][H] e4m3: the pairs' x rows, split exactly into hi + lo
+//   ret      [tl * K][H] fp32: the down-projection row of each of this rank's pairs
+enum : int { EP_EPOCH = 0, EP_DISP_COUNT = 1, EP_DOWN_COUNT = 2 };
+struct EpLayout {
+  size_t ctrl, rflag, rcount, retflag, rmeta, stage, ret, total;
+  int slots;  // pairs per source region
+};
+__host__ __device__ inline EpLayout ep_layout(int world, int tl, int K, int H) {
+  EpLayout A;
+  A.slots = tl * K;
+  size_t o = 0;
+  A.ctrl = o;
+  o += 64;
+  A.rflag = o;
+  o += 64;
+  A.rcount = o;
+  o += 64;
+  A.retflag = o;
+  o += 64;
+  A.rmeta = o = aup(o, 128);
+  o += static_cast<size_t>(world) * A.slots * 8;
+  A.stage = o = aup(o, 1024);
+  o += static_cast<size_t>(world) * A.slots * 2 * H;
+  A.ret = o = aup(o, 1024);
+  o += static_cast<size_t>(A.slots) * H * 4;
+  A.total = aup(o, 4096);
+  return A;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+// Waits (bounded) until the flag holds the epoch; false when the time limit ran out.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flagp, uint32_t epoch) {
+  if (ld_acquire_sys(flagp) == epoch) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_sys(flagp) != epoch) {
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    __nanosleep(100);
+  }
+  return true;
+}
+
 template <typename T>
 __device__ __forceinline__ T* ws_at(const Params& p, size_t off) {
   return reinterpret_cast<T*>(p.ws + off);
@@ -182,7 +254,7 @@ __global__ void __launch_bounds__(kLgThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sb + kLgSlabs * kLgBSlab);
   uint64_t* done = full + kLgSlabs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const Layout L = layout_of(p);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kRows, t0 = blockIdx.y * kLgTok, ks = blockIdx.z;
   const int nsl = min(kLgSlabs, p.H / 64 - ks * kLgSlabs);
@@ -312,7 +384,7 @@ __device__ __forceinline__ float logit_map(const Params& p, float v, int e) {
 // renormalised weights.
 __global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_constant__ Params p) {
   __shared__ SelSmem sm;
-  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const Layout L = layout_of(p);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t = blockIdx.x;
   const int H = p.H, E = p.E, K = p.K;
@@ -557,40 +629,103 @@ __device__ __forceinline__ void split_row(const Params& p, const Layout& L, int 
   }
 }
 
+// The received pairs of an expert-parallel destination, in (source rank, slot) order: pair r is
+// slot r - pre[s] of source s's region.
+struct RecvPairs {
+  int pre[kMaxRanks + 1];
+  __device__ __forceinline__ void locate(int r, int world, int& src, int& slot) const {
+    src = 0;
+#pragma unroll
+    for (int s = 1; s < kMaxRanks; ++s)
+      if (s < world && r >= pre[s]) src = s;
+    slot = r - pre[src];
+  }
+};
+
+// Copies a received pair's hi / lo rows from the staging area into position pos (one warp).
+__device__ __forceinline__ void copy_row(const Params& p, const Layout& L, const uint8_t* srow, int pos, int lane) {
+  uint8_t* drow = p.ws + L.pimg + static_cast<size_t>(2 * pos) * p.H;
+  const int n16 = 2 * p.H / 16;
+  constexpr int kC = 2 * kMaxH / 16 / 32;
+  uint4 v[kC];
+#pragma unroll
+  for (int i = 0; i < kC; ++i)
+    if (lane + 32 * i < n16) v[i] = __ldcg(reinterpret_cast<const uint4*>(srow) + lane + 32 * i);
+#pragma unroll
+  for (int i = 0; i < kC; ++i)
+    if (lane + 32 * i < n16) reinterpret_cast<uint4*>(drow)[lane + 32 * i] = v[i];
+}
+
 __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_constant__ Params p) {
   __shared__ int hist[kMaxRouter], before[kMaxRouter], off[kMaxRouter + 1], tbase[kMaxRouter + 1];
   __shared__ int spos[kMaxPpc];
-  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  __shared__ RecvPairs rp;
+  __shared__ int s_ok;
+  const Layout L = layout_of(p);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int E = p.E, K = p.K, T = p.T, P = T * K;
-  const int ppc = pairs_per_cta(P);
-  const int n_pair_ctas = (P + ppc - 1) / ppc;
+  const bool ep = p.world > 1;
+  const int K = p.K, T = p.T;
+  const int E = ep ? p.ep_el : p.E;  // experts whose tiles are built here
+  const int cap = L.cap;             // pair slots (single GPU: T * K)
+  const int ppc = pairs_per_cta(cap);
+  const int n_pair_ctas = (cap + ppc - 1) / ppc;
   griddep_wait();
   griddep_launch();
   if (static_cast<int>(blockIdx.x) >= n_pair_ctas) {
-    // the shared expert's positions: one warp per token
+    // the shared expert's positions: one warp per local token
     const int t = (blockIdx.x - n_pair_ctas) * kDispWarps + warp;
     if (p.sh_w13 != nullptr && t < T) {
-      if (lane == 0) ws_at<int>(p, L.pos_tok)[P + t] = t;
-      split_row(p, L, P + t, t, lane);
+      if (lane == 0) ws_at<int>(p, L.pos_tok)[cap + t] = t;
+      split_row(p, L, cap + t, t, lane);
     }
     return;
   }
-  const int a = blockIdx.x * ppc, b = min(P, a + ppc);
+  // the pairs: this rank's own (single GPU) or the ones every source rank sent here
+  const uint8_t* arena = ep ? p.ep_arena[p.rank] : nullptr;
+  const EpLayout A = ep_layout(p.world > 1 ? p.world : 1, p.ep_tl, K, p.H);
+  int R = cap;
+  if (ep) {
+    if (tid == 0) s_ok = 1;
+    __syncthreads();
+    const uint32_t epoch = __ldcg(reinterpret_cast<const uint32_t*>(arena + A.ctrl) + EP_EPOCH);
+    if (tid < p.world && !wait_epoch(reinterpret_cast<const uint32_t*>(arena + A.rflag) + tid, epoch)) {
+      flag(p, STATUS_TIMEOUT);
+      s_ok = 0;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0;
+      for (int s = 0; s <= kMaxRanks; ++s) {
+        rp.pre[s] = acc;
+        if (s < p.world && s_ok) acc += min(static_cast<int>(__ldcg(reinterpret_cast<const uint32_t*>(arena + A.rcount) + s)), A.slots);
+      }
+      if (!s_ok) rp.pre[kMaxRanks] = 0;
+    }
+    __syncthreads();
+    R = s_ok ? rp.pre[p.world] : 0;
+  }
+  const int2* rmeta = ep ? reinterpret_cast<const int2*>(arena + A.rmeta) : nullptr;
+  const int* pair_e = ws_at<const int>(p, L.pair_e);
+  auto expert_of = [&](int i) -> int {
+    if (!ep) return __ldcg(pair_e + i);
+    int src, slot;
+    rp.locate(i, p.world, src, slot);
+    return __ldcg(&rmeta[src * A.slots + slot].x) >> 20;
+  };
+  const int a = blockIdx.x * ppc, b = min(R, a + ppc);
   for (int e = tid; e < kMaxRouter; e += kDispThreads) {
     hist[e] = 0;
     before[e] = 0;
   }
   __syncthreads();
-  const int* pair_e = ws_at<const int>(p, L.pair_e);
-  for (int i0 = 4 * tid; i0 < P; i0 += 4 * kDispThreads) {
+  for (int i0 = 4 * tid; i0 < R; i0 += 4 * kDispThreads) {
     int ev[4];
-    if (i0 + 3 < P && (P & 3) == 0) {
+    if (!ep && i0 + 3 < R && (R & 3) == 0) {
       const int4 v = __ldcg(reinterpret_cast<const int4*>(pair_e + i0));
       ev[0] = v.x, ev[1] = v.y, ev[2] = v.z, ev[3] = v.w;
     } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) ev[u] = i0 + u < P ? __ldcg(pair_e + i0 + u) : -1;
+      for (int u = 0; u < 4; ++u) ev[u] = i0 + u < R ? expert_of(i0 + u) : -1;
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u)
@@ -640,7 +775,7 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_con
     int* inv = ws_at<int>(p, L.inv);
     for (int i0 = a; i0 < b; i0 += 32) {
       const int i = i0 + lane;
-      const int e = i < b ? __ldcg(pair_e + i) : -1;
+      const int e = i < b ? expert_of(i) : -1;
       const unsigned m = __match_any_sync(0xffffffffu, e);
       const int rank = e >= 0 ? before[e] + __popc(m & ((1u << lane) - 1u)) : 0;
       __syncwarp();
@@ -649,10 +784,12 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_con
       const int pos = e >= 0 ? off[e] + rank : -1;
       if (i < b) {
         spos[i - a] = pos;
-        inv[i] = pos;
-        if (pos >= 0) {
-          pos_tok[pos] = i / K;
-          if (p.perm_out) p.perm_out[pos] = i;
+        if (!ep) {
+          inv[i] = pos;
+          if (pos >= 0) {
+            pos_tok[pos] = i / K;
+            if (p.perm_out) p.perm_out[pos] = i;
+          }
         }
       }
     }
@@ -668,7 +805,7 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_con
         tiles[tbase[e] + j] = make_int4(e, off[e] + j * kTileTok, min(kTileTok, n - j * kTileTok), 0);
     }
     for (int j = tid; j < nt_sh; j += kDispThreads)
-      tiles[nt_routed + j] = make_int4(-1, P + j * kTileTok, min(kTileTok, T - j * kTileTok), 0);
+      tiles[nt_routed + j] = make_int4(-1, cap + j * kTileTok, min(kTileTok, T - j * kTileTok), 0);
     if (p.offsets_out)
       for (int e = tid; e <= E; e += kDispThreads) p.offsets_out[e] = off[e];
     if (tid == 0) {
@@ -680,7 +817,118 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_con
   // the permuted activation rows of this CTA's pairs
   for (int j = warp; j < b - a; j += kDispWarps) {
     const int pos = spos[j];
-    if (pos >= 0) split_row(p, L, pos, (a + j) / K, lane);
+    if (pos < 0) continue;
+    if (!ep) {
+      split_row(p, L, pos, (a + j) / K, lane);
+    } else {
+      int src, slot;
+      rp.locate(a + j, p.world, src, slot);
+      const int2 m = __ldcg(&rmeta[src * A.slots + slot]);
+      if (lane == 0) {
+        ws_at<float>(p, L.pxinv)[pos] = exp2i(-m.y);
+        ws_at<int>(p, L.pos_tok)[pos] = (src << 20) | (m.x & 0xFFFFF);  // where the output row goes
+      }
+      copy_row(p, L, arena + A.stage + (static_cast<size_t>(src) * A.slots + slot) * 2 * p.H, pos, lane);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ expert-parallel dispatch
+// Source side: every pair of this rank's tokens goes to the rank owning its expert. CTA c owns
+// pairs [a, b); it counts each destination's pairs (all, and those before a), ranks its own in
+// order within their destination, and writes each pair's split x rows and metadata into the
+// destination's stage / rmeta region of this source over NVLink. The last CTA to finish (counted on
+// a local counter after a system-scope fence by each CTA) writes every destination's count and then
+// its flag (the call's epoch, with a system-scope release), and advances the local epoch.
+__global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_constant__ Params p) {
+  __shared__ int dcount[kMaxRanks], dbefore[kMaxRanks];
+  __shared__ int spos[kMaxPpc];
+  __shared__ int s_last;
+  const Layout L = layout_of(p);
+  const EpLayout A = ep_layout(p.world, p.ep_tl, p.K, p.H);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = p.K, P = p.T * K, W = p.world, el = p.ep_el;
+  const int ppc = pairs_per_cta(P);
+  const int a = blockIdx.x * ppc, b = min(P, a + ppc);
+  uint32_t* own_ctrl = reinterpret_cast<uint32_t*>(p.ep_arena[p.rank] + A.ctrl);
+  griddep_wait();
+  griddep_launch();
+  const uint32_t epoch = __ldcg(own_ctrl + EP_EPOCH) + 1u;
+  if (tid < kMaxRanks) {
+    dcount[tid] = 0;
+    dbefore[tid] = 0;
+  }
+  __syncthreads();
+  const int* pair_e = ws_at<const int>(p, L.pair_e);
+  for (int i = tid; i < P; i += kDispThreads) {
+    const int d = __ldcg(pair_e + i) / el;
+    atomicAdd(&dcount[d], 1);
+    if (i < a) atomicAdd(&dbefore[d], 1);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int i0 = a; i0 < b; i0 += 32) {
+      const int i = i0 + lane;
+      const int d = i < b ? __ldcg(pair_e + i) / el : -1;
+      const unsigned m = __match_any_sync(0xffffffffu, d);
+      const int rank = d >= 0 ? dbefore[d] + __popc(m & ((1u << lane) - 1u)) : 0;
+      __syncwarp();
+      if (d >= 0 && lane == __ffs(m) - 1) dbefore[d] += __popc(m);
+      __syncwarp();
+      if (i < b) spos[i - a] = (d << 24) | rank;
+    }
+  }
+  __syncthreads();
+  for (int j = warp; j < b - a; j += kDispWarps) {
+    const int i = a + j, t = i / K;
+    const int d = spos[j] >> 24, slot = spos[j] & 0xFFFFFF;
+    const int e = __ldcg(pair_e + i);
+    uint8_t* dst_arena = p.ep_arena[d];
+    const size_t sidx = static_cast<size_t>(p.rank) * A.slots + slot;
+    const int ex = __ldcg(ws_at<const int>(p, L.xexp) + t);
+    if (lane == 0) reinterpret_cast<int2*>(dst_arena + A.rmeta)[sidx] = make_int2(((e - d * el) << 20) | i, ex);
+    const float sc = exp2i(ex);
+    const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
+    uint8_t* hi_row = dst_arena + A.stage + sidx * 2 * p.H;
+    uint8_t* lo_row = hi_row + p.H;
+    constexpr int kC = kMaxH / 16 / 32;
+    uint4 v[kC][2];
+#pragma unroll
+    for (int c0 = 0; c0 < kC; ++c0) {
+      const int c = lane + 32 * c0;
+      if (c < p.H / 16) {
+        v[c0][0] = __ldg(src + 2 * c);
+        v[c0][1] = __ldg(src + 2 * c + 1);
+      }
+    }
+#pragma unroll
+    for (int c0 = 0; c0 < kC; ++c0) {
+      const int c = lane + 32 * c0;
+      if (c < p.H / 16) {
+        uint4 hi, lo;
+        split16(v[c0], sc, hi, lo);
+        *reinterpret_cast<uint4*>(hi_row + 16 * c) = hi;
+        *reinterpret_cast<uint4*>(lo_row + 16 * c) = lo;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence_system();  // cumulative: this CTA's peer writes, seen through the barrier
+    s_last = atomicAdd(own_ctrl + EP_DISP_COUNT, 1u) == gridDim.x - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (s_last) {
+    if (tid < W) {
+      __threadfence_system();
+      uint8_t* dst_arena = p.ep_arena[tid];
+      reinterpret_cast<uint32_t*>(dst_arena + A.rcount)[p.rank] = static_cast<uint32_t>(dcount[tid]);
+      st_release_sys(reinterpret_cast<uint32_t*>(dst_arena + A.rflag) + p.rank, epoch);
+    }
+    if (tid == 0) {
+      own_ctrl[EP_DISP_COUNT] = 0u;
+      own_ctrl[EP_EPOCH] = epoch;
+    }
   }
 }
 
@@ -694,6 +942,7 @@ struct Aux {
   uint64_t mma_done;
   uint32_t tmem;
   int abort;
+  int last;  // expert parallel, down: this CTA finished last
   float amax[2][2][4][32];  // up: [item parity][token half][lane quarter][token] |h| maxima
 };
 
@@ -720,7 +969,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kBOff = 2 * kSlab;  // activation slab inside a stage
   constexpr uint32_t kAccCols = 256;
   Aux& aux = *reinterpret_cast<Aux*>(smem + kStages * kStage);
-  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const Layout L = layout_of(p);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // items: up 128 gate rows + the matching 128 up rows; down 256 output rows (two 128-row halves)
   const int nrb = DOWN ? p.H / (2 * kRows) : p.I / kRows;
@@ -838,11 +1087,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (DOWN) griddep_wait();  // the h blocks' scales come from the up kernel
     // per-item token data, fetched one item ahead: up 2^-e of each token's x split, down the
     // token's 2^-e of each 128-block of h
-    auto token_data = [&](const int4& it, float (&v)[kMaxI / 128]) {
+    // (down, expert parallel: the token's output row destination, source rank << 20 | pair index)
+    auto token_data = [&](const int4& it, float (&v)[kMaxI / 128], int& rm) {
       const int nh = min(max(it.z - 32 * hf, 0), 32);
       const int pos = it.y + 32 * hf + lane;
 #pragma unroll
       for (int kb = 0; kb < kMaxI / 128; ++kb) v[kb] = 0.f;
+      rm = -1;
       if (lane < nh) {
         if (!DOWN) {
           v[0] = __ldcg(ws_at<const float>(p, L.pxinv) + pos);
@@ -850,6 +1101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kb = 0; kb < kMaxI / 128; ++kb)
             if (kb < nkb) v[kb] = __ldcg(ws_at<const float>(p, L.hinv) + static_cast<size_t>(pos) * nkb + kb);
+          if (p.world > 1 && it.x >= 0) rm = __ldcg(ws_at<const int>(p, L.pos_tok) + pos);
         }
       }
     };
@@ -869,9 +1121,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int use = 0;
     int4 it_next = my_items > 0 ? item_desc(aux, tiles, nrb, 0) : make_int4(0, 0, 0, 0);
     float td_next[kMaxI / 128];
+    int rm_next = -1;
     float sg_next = 0.f, su_next = 0.f;  // the next item's first-slab scales
     if (my_items > 0) {
-      token_data(it_next, td_next);
+      token_data(it_next, td_next, rm_next);
       sg_next = __ldg(scale_row(it_next, false));
       su_next = __ldg(scale_row(it_next, true));
     }
@@ -881,9 +1134,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kMaxI / 128; ++i) td[i] = td_next[i];
       float sg = sg_next, su = su_next;
+      const int rm = rm_next;
       if (k + 1 < my_items) {
         it_next = item_desc(aux, tiles, nrb, k + 1);
-        token_data(it_next, td_next);
+        token_data(it_next, td_next, rm_next);
         sg_next = __ldg(scale_row(it_next, false));
         su_next = __ldg(scale_row(it_next, true));
       }
@@ -1017,13 +1271,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (q == 0 && lane < nh)
           ws_at<float>(p, L.hinv)[static_cast<size_t>(pbase + lane) * (p.I / 128) + it.w] = exp2i(-e_mine);
       } else {
-        float* out = ws_at<float>(p, L.outp) + static_cast<size_t>(pbase) * p.H + 2 * kRows * it.w + r;
+        const int col = 2 * kRows * it.w + r;
+        if (p.world > 1 && !shared_tile) {
+          // expert parallel: each row goes straight to its source rank's return buffer over NVLink
+          const EpLayout A = ep_layout(p.world, p.ep_tl, p.K, p.H);
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j < nh) {
-            __stcg(out + static_cast<size_t>(j) * p.H, a0[j]);
-            __stcg(out + static_cast<size_t>(j) * p.H + kRows, a1[j]);
+          for (int j = 0; j < 32; ++j) {
+            const int rmj = __shfl_sync(0xffffffffu, rm, j);
+            if (j < nh) {
+              float* out = reinterpret_cast<float*>(p.ep_arena[rmj >> 20] + A.ret) +
+                           static_cast<size_t>(rmj & 0xFFFFF) * p.H + col;
+              __stcg(out, a0[j]);
+              __stcg(out + kRows, a1[j]);
+            }
           }
+        } else {
+          float* out = ws_at<float>(p, L.outp) + static_cast<size_t>(pbase) * p.H + col;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nh) {
+              __stcg(out + static_cast<size_t>(j) * p.H, a0[j]);
+              __stcg(out + static_cast<size_t>(j) * p.H + kRows, a1[j]);
+            }
+        }
       }
     }
   }
@@ -1032,6 +1302,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
+  if (DOWN && p.world > 1) {
+    // the last CTA tells every source rank that its output rows have landed: a system-scope fence
+    // per CTA (cumulative over the CTA's stores, ordered by the barrier above), a local counter,
+    // then a release of the call's epoch into each source's retflag
+    const EpLayout A = ep_layout(p.world, p.ep_tl, p.K, p.H);
+    uint32_t* own_ctrl = reinterpret_cast<uint32_t*>(p.ep_arena[p.rank] + A.ctrl);
+    if (tid == 0) {
+      __threadfence_system();
+      aux.last = atomicAdd(own_ctrl + EP_DOWN_COUNT, 1u) == gridDim.x - 1 ? 1 : 0;
+    }
+    __syncthreads();
+    if (aux.last) {
+      const uint32_t epoch = __ldcg(own_ctrl + EP_EPOCH);
+      if (tid < p.world) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t*>(p.ep_arena[tid] + A.retflag) + p.rank, epoch);
+      }
+      if (tid == 0) own_ctrl[EP_DOWN_COUNT] = 0u;
+    }
+  }
 }
 
 // ------------------------------------------------------------------ combine kernel
@@ -1039,7 +1329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // rounding points of fp8_moe_forward's bf16 output, the speaker's bias add (engine.py:237) and
 // speaker_forward's bf16 tensor sum (engine.py:158). One thread per 8 outputs.
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_constant__ Params p) {
-  const Layout L = layout(p.T, p.H, p.I, p.E, p.K);
+  const Layout L = layout_of(p);
   const int c8 = p.H / 8;
   const int g = blockIdx.x * kCombineThreads + threadIdx.x;
   const int t = g / c8, n = (g % c8) * 8;
@@ -1051,21 +1341,34 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
   }
   griddep_wait();
   griddep_launch();
+  const bool ep = p.world > 1;
+  const EpLayout A = ep_layout(ep ? p.world : 1, p.ep_tl, p.K, p.H);
+  if (ep) {
+    // every destination rank has written this rank's output rows (bounded wait on its flag; a wait
+    // that runs out is reported in the status word)
+    const uint8_t* arena = p.ep_arena[p.rank];
+    const uint32_t epoch = __ldcg(reinterpret_cast<const uint32_t*>(arena + A.ctrl) + EP_EPOCH);
+    if (threadIdx.x < p.world && !wait_epoch(reinterpret_cast<const uint32_t*>(arena + A.retflag) + threadIdx.x, epoch))
+      flag(p, STATUS_TIMEOUT);
+    __syncthreads();
+  }
   if (!active) return;
   const int K = p.K;
   int pos[kMaxTopK];
   float w[kMaxTopK];
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j) {
-    pos[j] = j < K ? __ldcg(ws_at<const int>(p, L.inv) + t * K + j) : -1;
+    // expert parallel: pair t * K + j's row is row t * K + j of the return buffer
+    pos[j] = j < K ? (ep ? t * K + j : __ldcg(ws_at<const int>(p, L.inv) + t * K + j)) : -1;
     w[j] = j < K ? __ldcg(ws_at<const float>(p, L.pair_w) + t * K + j) : 0.f;
   }
   const float* outp = ws_at<const float>(p, L.outp);
+  const float* rows = ep ? reinterpret_cast<const float*>(p.ep_arena[p.rank] + A.ret) : outp;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < kMaxTopK; ++j) {
     if (pos[j] >= 0) {
-      const float4* row = reinterpret_cast<const float4*>(outp + static_cast<size_t>(pos[j]) * p.H + n);
+      const float4* row = reinterpret_cast<const float4*>(rows + static_cast<size_t>(pos[j]) * p.H + n);
       const float4 o0 = __ldcg(row), o1 = __ldcg(row + 1);
       acc[0] = fmaf(w[j], o0.x, acc[0]), acc[1] = fmaf(w[j], o0.y, acc[1]), acc[2] = fmaf(w[j], o0.z, acc[2]);
       acc[3] = fmaf(w[j], o0.w, acc[3]), acc[4] = fmaf(w[j], o1.x, acc[4]), acc[5] = fmaf(w[j], o1.y, acc[5]);
@@ -1076,7 +1379,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
   float shv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float gate = 0.f;
   if (sh) {
-    const float4* row = reinterpret_cast<const float4*>(outp + static_cast<size_t>(p.T * K + t) * p.H + n);
+    const float4* row = reinterpret_cast<const float4*>(outp + static_cast<size_t>(L.cap + t) * p.H + n);
     const float4 o0 = __ldcg(row), o1 = __ldcg(row + 1);
     shv[0] = o0.x, shv[1] = o0.y, shv[2] = o0.z, shv[3] = o0.w, shv[4] = o1.x, shv[5] = o1.y, shv[6] = o1.z, shv[7] = o1.w;
     gate = __ldcg(ws_at<const float>(p, L.gate) + t);
@@ -1128,11 +1431,13 @@ constexpr size_t kExpertSmem(bool) {
 size_t prefill_ws_bytes(int T, int H, int I, int E, int K) { return pf::layout(T, H, I, E, K).total; }
 
 // Launches the prefill chain; route = false starts at the select kernel (routing given).
-int launch_prefill(const pf::Params& p, cudaStream_t stream) {
+// phases: 1 = routing and (expert parallel) sending the pairs to their owners; 2 = dispatch into
+// expert tiles, the expert products, (expert parallel) returning the rows, combine.
+int launch_prefill(const pf::Params& p, cudaStream_t stream, int phases = 3) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = sm_count(dev);
-  const pf::Layout L = pf::layout(p.T, p.H, p.I, p.E, p.K);
+  const pf::Layout L = pf::layout_of(p);
   static bool attrs_set = false;
   if (!attrs_set) {
     cudaFuncSetAttribute(pf::logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem);
@@ -1143,37 +1448,50 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream) {
     attrs_set = true;
   }
   const int H = p.H, I = p.I, E = p.E;
+  const int E_w = p.world > 1 ? p.ep_el : E;  // experts held by this rank's weight tensors
   const uint64_t rows2 = static_cast<uint64_t>(2) * L.npos;
   CUtensorMap mr, mx, m13, msh13, m2, msh2, mb_up[4], mb_dn[4];
   bool ok = true;
-  if (p.mode == 1) {
+  if (p.mode == 1 && (phases & 1)) {
     ok = ok && tensor_map_3d(&mr, p.router_w, 2ull * H, E, 1, 2ull * H, 2ull * H * E, 128);
     ok = ok && tensor_map_3d(&mx, p.x, 2ull * H, p.T, 1, 2ull * H, 2ull * H * p.T, pf::kLgTok);
   }
-  ok = ok && tensor_map_3d(&m13, p.w13, H, 2ull * I, E, H, p.w13_stride, 128);
-  ok = ok && tensor_map_3d(&m2, p.w2, I, H, E, I, p.w2_stride, 128);
-  if (p.sh_w13) {
+  if (phases & 2) ok = ok && tensor_map_3d(&m13, p.w13, H, 2ull * I, E_w, H, p.w13_stride, 128);
+  if (phases & 2) ok = ok && tensor_map_3d(&m2, p.w2, I, H, E_w, I, p.w2_stride, 128);
+  if (p.sh_w13 && (phases & 2)) {
     ok = ok && tensor_map_3d(&msh13, p.sh_w13, H, 2ull * I, 1, H, 2ull * I * H, 128);
     ok = ok && tensor_map_3d(&msh2, p.sh_w2, I, H, 1, I, static_cast<uint64_t>(H) * I, 128);
   } else {
     msh13 = m13;
     msh2 = m2;
   }
-  for (int b = 0; b < 4; ++b) {
+  for (int b = 0; b < 4 && (phases & 2); ++b) {
     ok = ok && tensor_map_3d(&mb_up[b], p.ws + L.pimg, H, rows2, 1, H, rows2 * H, 16u << b);
     ok = ok && tensor_map_3d(&mb_dn[b], p.ws + L.himg, I, rows2, 1, I, rows2 * I, 16u << b);
   }
   if (!ok) return 2;
   int n = 0;
-  if (p.mode == 1) {
-    const dim3 g((E + pf::kRows - 1) / pf::kRows, (p.T + pf::kLgTok - 1) / pf::kLgTok, L.ks);
-    if (pf_launch(pf::logits_kernel, g, pf::kLgThreads, pf::kLgSmem, stream, "prefill logits", p, mr, mx)) return 2;
+  if (phases & 1) {
+    if (p.mode == 1) {
+      const dim3 g((E + pf::kRows - 1) / pf::kRows, (p.T + pf::kLgTok - 1) / pf::kLgTok, L.ks);
+      if (pf_launch(pf::logits_kernel, g, pf::kLgThreads, pf::kLgSmem, stream, "prefill logits", p, mr, mx)) return 2;
+      ++n;
+    }
+    if (pf_launch(pf::select_kernel, dim3(p.T), pf::kSelThreads, 0, stream, "prefill select", p)) return 2;
     ++n;
+    if (p.world > 1) {
+      const int P = p.T * p.K;
+      if (pf_launch(pf::ep_dispatch_kernel, dim3((P + pf::pairs_per_cta(P) - 1) / pf::pairs_per_cta(P)),
+                    pf::kDispThreads, 0, stream, "expert-parallel dispatch", p))
+        return 2;
+      ++n;
+    }
   }
-  if (pf_launch(pf::select_kernel, dim3(p.T), pf::kSelThreads, 0, stream, "prefill select", p))
-    return 2;
-  const int P = p.T * p.K;
-  const int disp_ctas = (P + pf::pairs_per_cta(P) - 1) / pf::pairs_per_cta(P) +
+  if (!(phases & 2)) {
+    note_launches(n);
+    return 0;
+  }
+  const int disp_ctas = (L.cap + pf::pairs_per_cta(L.cap) - 1) / pf::pairs_per_cta(L.cap) +
                         (p.sh_w13 ? (p.T + pf::kDispWarps - 1) / pf::kDispWarps : 0);
   if (pf_launch(pf::dispatch_kernel, dim3(disp_ctas), pf::kDispThreads, 0, stream, "prefill dispatch", p)) return 2;
   if (pf_launch(pf::expert_kernel<false>, dim3(sms), pf::kThreads, kExpertSmem(false), stream, "prefill up", p, m13,
@@ -1186,13 +1504,13 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream) {
   if (pf_launch(pf::combine_kernel, dim3((c_threads + pf::kCombineThreads - 1) / pf::kCombineThreads),
                 pf::kCombineThreads, 0, stream, "prefill combine", p))
     return 2;
-  note_launches(n + 5);
+  note_launches(n + 4);
   return 0;
 }
 
 // Router only: logits + select (ids_out / w_out).
 int launch_route(const pf::Params& p, cudaStream_t stream) {
-  const pf::Layout L = pf::layout(p.T, p.H, p.I, p.E, p.K);
+  const pf::Layout L = pf::layout_of(p);
   static bool attrs_set = false;
   if (!attrs_set) {
     cudaFuncSetAttribute(pf::logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::kLgSmem);
@@ -1358,4 +1676,165 @@ extern "C" int dm3_route(const void* x, int T, int H, const void* router_w, int 
   p.w_out = static_cast<__nv_bfloat16*>(w_out);
   p.ws = static_cast<uint8_t*>(workspace);
   return dm3::launch_route(p, static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------ expert-parallel C ABI
+extern "C" size_t dm3_ep_arena_bytes(int world, int tokens_per_rank, int top_k, int H) {
+  if (world < 2 || world > dm3::pf::kMaxRanks || tokens_per_rank < 1 || top_k < 1 || H < 128) return 0;
+  return dm3::pf::ep_layout(world, tokens_per_rank, top_k, H).total;
+}
+
+extern "C" int dm3_ep_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return dm3::set_error("dm3_ep_alloc: bad arguments"), 1;
+  *ptr = nullptr;
+  cudaError_t err = cudaMalloc(ptr, bytes);
+  if (err == cudaSuccess) err = cudaMemset(*ptr, 0, bytes);
+  if (err != cudaSuccess) return dm3::set_error(std::string("dm3_ep_alloc: ") + cudaGetErrorString(err)), 2;
+  return 0;
+}
+
+extern "C" int dm3_ep_free(void* ptr) {
+  if (ptr && cudaFree(ptr) != cudaSuccess) return dm3::set_error("dm3_ep_free failed"), 2;
+  return 0;
+}
+
+extern "C" int dm3_ep_ipc_handle(void* ptr, void* handle_out) {
+  if (!ptr || !handle_out) return dm3::set_error("dm3_ep_ipc_handle: null argument"), 1;
+  cudaIpcMemHandle_t h;
+  const cudaError_t err = cudaIpcGetMemHandle(&h, ptr);
+  if (err != cudaSuccess) return dm3::set_error(std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(err)), 2;
+  std::memcpy(handle_out, &h, sizeof(h));
+  return 0;
+}
+
+extern "C" int dm3_ep_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return dm3::set_error("dm3_ep_ipc_open: null argument"), 1;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return dm3::set_error(std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(err)), 2;
+  return 0;
+}
+
+extern "C" int dm3_ep_ipc_close(void* ptr) {
+  if (ptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) return dm3::set_error("cudaIpcCloseMemHandle failed"), 2;
+  return 0;
+}
+
+extern "C" size_t dm3_moe_prefill_ep_workspace_bytes(int world, int tokens_per_rank, int H, int I, int n_router,
+                                                     int top_k) {
+  if (world < 2 || world > dm3::pf::kMaxRanks || tokens_per_rank < 1 || H < 128 || I < 128 || n_router < 1 ||
+      top_k < 1)
+    return 0;
+  return dm3::pf::layout(tokens_per_rank, H, I, n_router, top_k, world * tokens_per_rank * top_k).total;
+}
+
+namespace {
+
+int check_ep(int world, int rank, int T, int tokens_per_rank, int n_router, void* const* arenas) {
+  if (world < 2 || world > dm3::pf::kMaxRanks) return dm3::set_error("world must be in [2, 8]"), 1;
+  if (rank < 0 || rank >= world) return dm3::set_error("rank out of range"), 1;
+  if (T > tokens_per_rank) return dm3::set_error("T exceeds the arena's tokens per rank"), 1;
+  if (n_router % world) return dm3::set_error("the expert count must divide evenly over the ranks"), 1;
+  if (static_cast<int64_t>(world) * tokens_per_rank * 8 > 256 * dm3::pf::kMaxPpc)
+    return dm3::set_error("world * tokens_per_rank * top_k exceeds the dispatch capacity"), 1;
+  if (!arenas) return dm3::set_error("arena pointers are required"), 1;
+  for (int r = 0; r < world; ++r)
+    if (!arenas[r] || (reinterpret_cast<uintptr_t>(arenas[r]) & 4095u)) return dm3::set_error("bad arena pointer"), 1;
+  return 0;
+}
+
+void set_ep(dm3::pf::Params& p, int world, int rank, int tokens_per_rank, void* const* arenas) {
+  p.world = world;
+  p.rank = rank;
+  p.ep_tl = tokens_per_rank;
+  p.ep_el = p.E / world;
+  for (int r = 0; r < dm3::pf::kMaxRanks; ++r) p.ep_arena[r] = r < world ? static_cast<uint8_t*>(arenas[r]) : nullptr;
+}
+
+}  // namespace
+
+// phases as launch_prefill: 1 = ep_dispatch, 2 = ep_combine, 3 = both
+static int prefill_ep(int phases, const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                      int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride, const float* s13,
+                      int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride,
+                      int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
+                      int sh_srows, const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out,
+                      void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  dm3::note_launches(0);
+  int rc = check_ep(world, rank, T, tokens_per_rank, n_router, arenas);
+  if (rc) return rc;
+  // expert weights are only read by the second phase; the checks below take any non-null
+  // placeholders for the first
+  rc = check_prefill(T, H, I, n_router, top_k, x, w13, w13_stride, s13, w2, w2_stride, s2, srows, y, workspace,
+                     SIZE_MAX);
+  if (rc) return rc;
+  if (workspace_bytes < dm3_moe_prefill_ep_workspace_bytes(world, tokens_per_rank, H, I, n_router, top_k))
+    return dm3::set_error("workspace too small"), 4;
+  if (!router_w || !al16(router_w)) return dm3::set_error("router weight (bf16) must be given, 16-byte aligned"), 1;
+  if (out_bias && !al16(out_bias)) return dm3::set_error("out_bias must be 16-byte aligned"), 1;
+  if (sh_w13) {
+    if (!sh_s13 || !sh_w2 || !sh_s2) return dm3::set_error("shared expert needs w13, s13, w2, s2"), 1;
+    if (!al16(sh_w13) || !al16(sh_w2)) return dm3::set_error("shared expert weights must be 16-byte aligned"), 1;
+    if (sh_srows != 1 && sh_srows != 128) return dm3::set_error("sh_srows must be 1 or 128"), 1;
+    if (sh_gate && !al16(sh_gate)) return dm3::set_error("shared gate must be 16-byte aligned"), 1;
+  }
+  dm3::pf::Params p = prefill_params(x, T, H, I, n_router, top_k, w13, w13_stride, s13, s13_stride, w2, w2_stride, s2,
+                                     s2_stride, srows, y, nullptr, nullptr, workspace);
+  p.mode = 1;
+  p.router_w = static_cast<const __nv_bfloat16*>(router_w);
+  p.logits_bf16 = logits_bf16;
+  p.logit_bias = logit_bias;
+  p.sh_w13 = static_cast<const uint8_t*>(sh_w13);
+  p.sh_s13 = sh_s13;
+  p.sh_w2 = static_cast<const uint8_t*>(sh_w2);
+  p.sh_s2 = sh_s2;
+  p.sh_srows = sh_w13 ? sh_srows : 128;
+  p.sh_gate = sh_w13 ? static_cast<const __nv_bfloat16*>(sh_gate) : nullptr;
+  p.out_bias = out_bias;
+  p.ids_out = ids_out;
+  p.w_out = static_cast<__nv_bfloat16*>(w_out);
+  set_ep(p, world, rank, tokens_per_rank, arenas);
+  return dm3::launch_prefill(p, static_cast<cudaStream_t>(stream), phases);
+}
+
+extern "C" int dm3_moe_prefill_ep(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                                  int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
+                                  const float* s13, int64_t s13_stride, const void* w2, int64_t w2_stride,
+                                  const float* s2, int64_t s2_stride, int srows, const void* sh_w13,
+                                  const float* sh_s13, const void* sh_w2, const float* sh_s2, int sh_srows,
+                                  const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
+                                  int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  return prefill_ep(3, x, T, H, I, router_w, n_router, top_k, logits_bf16, logit_bias, w13, w13_stride, s13,
+                    s13_stride, w2, w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows, sh_gate,
+                    out_bias, y, ids_out, w_out, world, rank, tokens_per_rank, arenas, workspace, workspace_bytes,
+                    stream);
+}
+
+extern "C" int dm3_ep_dispatch(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                               int logits_bf16, const float* logit_bias, const void* sh_gate, int64_t* ids_out,
+                               void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  // the expert operands are not read by this phase: the router weight stands in for them in the
+  // argument checks (and, when the shared gate is given, for the shared expert's presence)
+  return prefill_ep(1, x, T, H, I, router_w, n_router, top_k, logits_bf16, logit_bias, router_w, 2LL * I * H,
+                    reinterpret_cast<const float*>(router_w), 0, router_w, static_cast<int64_t>(H) * I,
+                    reinterpret_cast<const float*>(router_w), 0, 128, sh_gate ? router_w : nullptr,
+                    reinterpret_cast<const float*>(router_w), router_w, reinterpret_cast<const float*>(router_w), 128,
+                    sh_gate, nullptr, const_cast<void*>(x), ids_out, w_out, world, rank, tokens_per_rank, arenas,
+                    workspace, workspace_bytes, stream);
+}
+
+extern "C" int dm3_ep_combine(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                              const void* w13, int64_t w13_stride, const float* s13, int64_t s13_stride,
+                              const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride, int srows,
+                              const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
+                              int sh_srows, const void* sh_gate, const float* out_bias, void* y, int world, int rank,
+                              int tokens_per_rank, void* const* arenas, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  return prefill_ep(2, x, T, H, I, router_w, n_router, top_k, 1, nullptr, w13, w13_stride, s13, s13_stride, w2,
+                    w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows, sh_gate, out_bias, y,
+                    nullptr, nullptr, world, rank, tokens_per_rank, arenas, workspace, workspace_bytes, stream);
 }

@@ -214,6 +214,58 @@ int dm3_route(const void* x, int T, int H, const void* router_w, int n_router, i
               const float* logit_bias, int64_t* ids_out, void* w_out, void* workspace, size_t workspace_bytes,
               void* stream);
 
+/*
+ * Expert-parallel prefill over `world` ranks (one process per GPU, 2 <= world <= 8): rank r owns
+ * the experts [r * n_router / world, (r + 1) * n_router / world) and routes its own T <= tokens_per_rank
+ * tokens over all n_router experts. Each rank allocates one arena (dm3_ep_alloc of
+ * dm3_ep_arena_bytes), exports it (dm3_ep_ipc_handle, 64 bytes), and opens every other rank's handle
+ * (dm3_ep_ipc_open); `arenas` is the host array of the world arena pointers as mapped in this
+ * process (arenas[rank] its own). Pairs travel to their owner and output rows back over NVLink peer
+ * stores from inside the kernels, with flags carrying a per-call epoch (bounded waits; a wait that
+ * runs out sets the status word). Every rank must make the same sequence of calls.
+ * The SURVEY's NCCL all_to_all_single dispatch / combine of OnDemandExperts (engine.py:138-147) is
+ * replaced by these calls.
+ */
+size_t dm3_ep_arena_bytes(int world, int tokens_per_rank, int top_k, int H);
+int dm3_ep_alloc(size_t bytes, void** ptr);
+int dm3_ep_free(void* ptr);
+int dm3_ep_ipc_handle(void* ptr, void* handle_out);
+int dm3_ep_ipc_open(const void* handle, void** ptr);
+int dm3_ep_ipc_close(void* ptr);
+size_t dm3_moe_prefill_ep_workspace_bytes(int world, int tokens_per_rank, int H, int I, int n_router, int top_k);
+
+/*
+ * The prefill layer of dm3_moe_prefill under expert parallelism: x, y, ids_out, w_out are this
+ * rank's T tokens; w13 / s13 / w2 / s2 hold this rank's n_router / world experts (local index
+ * order); the router weight, logit bias and shared expert are replicated. The result equals
+ * dm3_moe_prefill on the concatenated tokens.
+ */
+int dm3_moe_prefill_ep(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                       int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride, const float* s13,
+                       int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride,
+                       int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
+                       int sh_srows, const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
+                       int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/*
+ * The two halves of dm3_moe_prefill_ep. dm3_ep_dispatch routes this rank's tokens and sends every
+ * (token, k) pair's exact e4m3 hi / lo rows to the rank owning its expert. dm3_ep_combine takes
+ * the pairs every rank sent here into expert tiles, runs this rank's experts, sends each output row
+ * back to its source rank, and combines this rank's tokens (+ shared expert, + bias). Call them in
+ * this order on the same stream with the same workspace; sh_gate must be given to both or neither.
+ */
+int dm3_ep_dispatch(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                    int logits_bf16, const float* logit_bias, const void* sh_gate, int64_t* ids_out, void* w_out,
+                    int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
+                    size_t workspace_bytes, void* stream);
+int dm3_ep_combine(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
+                   const void* w13, int64_t w13_stride, const float* s13, int64_t s13_stride, const void* w2,
+                   int64_t w2_stride, const float* s2, int64_t s2_stride, int srows, const void* sh_w13,
+                   const float* sh_s13, const void* sh_w2, const float* sh_s2, int sh_srows, const void* sh_gate,
+                   const float* out_bias, void* y, int world, int rank, int tokens_per_rank, void* const* arenas,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* Number of kernels the last MoE / GEMV entry point launched on this host thread. */
 int dm3_last_launch_count(void);
 

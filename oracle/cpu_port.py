@@ -26,9 +26,12 @@ def _deq(q: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
 
 
 def decode_layer(x: torch.Tensor, layer: dict, top_k: int = 8) -> torch.Tensor:
-    """One decode MoE layer (rows x [T, H] bf16) on the CPU in torch fp32."""
+    """One MoE layer over rows x [T, H] bf16 on the CPU in torch fp32: 2 decode rows, or the
+    hundreds of a prompt (prefill), with an optional per-expert logit bias."""
     gate = layer["gate"]
     logits = F.linear(x, gate) if gate.dtype == BF16 else x.float() @ gate.T  # bf16 / fp32 (speaker) router
+    if "logit_bias" in layer:  # the prefill router's per-expert bias, added to the logits before softmax
+        logits = logits.float() + layer["logit_bias"]
     probs = torch.softmax(logits.float(), -1)
     w, ids = probs.topk(top_k, -1)
     w = (w / w.sum(-1, keepdim=True)).to(BF16)
