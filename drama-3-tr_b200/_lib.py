@@ -49,8 +49,8 @@ SIGNATURES = {
     "dm3_ep_ipc_close": (_i, [_p]),
     "dm3_moe_prefill_ep_workspace_bytes": (_sz, [_i, _i, _i, _i, _i, _i]),
     "dm3_moe_prefill_ep": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p,
-                                _p, _p, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
-    "dm3_ep_dispatch": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
+                                _p, _p, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p, _sz, _p]),
+    "dm3_ep_dispatch": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p, _sz, _p]),
     "dm3_ep_combine": (_i, [_p, _i, _i, _i, _p, _i, _i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p, _p, _p,
                             _i, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
     "dm3_last_launch_count": (_i, []),

@@ -46,9 +46,12 @@ namespace pf {
 constexpr int kTileTok = 64;                 // tokens per expert tile
 constexpr int kRows = 128;                   // weight rows per MMA tile (M)
 constexpr int kSlab = kRows * 128;           // one 128-byte K slab of a 128-row tile
-constexpr int kThreads = 320;                // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+// warp 0 TMA, warp 1 MMA, then groups of 8 epilogue warps: the up kernel has two groups that take
+// alternate items, so one group's SwiGLU tail overlaps the other group's accumulator reads
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
+__host__ __device__ constexpr int epi_groups(bool down) { return down ? 1 : 2; }
+__host__ __device__ constexpr int expert_threads(bool down) { return 64 + epi_groups(down) * kEpiThreads; }
 constexpr int kStages = 4;                   // ring of TMA stages
 constexpr int kStage = 3 * kSlab;            // two weight slabs, the activation slab (<= 128 rows)
 constexpr int kNacc = 2;                     // TMEM accumulator buffers of 256 columns
@@ -59,7 +62,7 @@ constexpr int kLgThreads = 192;              // warp 0 TMA + MMA, warp 1 TMEM, w
 constexpr int kLgBSlab = kLgTok * 128;
 constexpr int kLgSmem = kLgSlabs * (kSlab + kLgBSlab) + 1024 + 256;
 constexpr int kCombineThreads = 256;
-constexpr int kBarEpi = 1;                   // named barrier of the up epilogue's warps
+constexpr int kBarEpi = 1;                   // named barriers of the up epilogue groups (1, 2)
 
 // control words; the status word sits where the decode workspace keeps it, so one reader serves both
 enum : int { C_STATUS = 4, C_NTILES = 8, C_NVALID = 9, C_WORDS = 16 };
@@ -102,7 +105,14 @@ struct Params {
   // arena mapped in this process (ep_arena[rank] its own), ep_tl the token capacity of every rank
   int world, rank, ep_tl, ep_el;
   uint8_t* ep_arena[kMaxRanks];
+  // optional placement [E]: (owning rank << 16) | index among that rank's experts; null places
+  // expert e on rank e / el at index e % el
+  const int* ep_owner;
 };
+
+__device__ __forceinline__ int ep_place(const Params& p, int e) {
+  return p.ep_owner ? __ldg(p.ep_owner + e) : ((e / p.ep_el) << 16) | (e % p.ep_el);
+}
 
 // ------------------------------------------------------------------ workspace layout
 // Positions: the P = T * K routed (token, k) pairs in dispatch order (expert-major, stable), then
@@ -847,7 +857,7 @@ __global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_
   const Layout L = layout_of(p);
   const EpLayout A = ep_layout(p.world, p.ep_tl, p.K, p.H);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = p.K, P = p.T * K, W = p.world, el = p.ep_el;
+  const int K = p.K, P = p.T * K, W = p.world;
   const int ppc = pairs_per_cta(P);
   const int a = blockIdx.x * ppc, b = min(P, a + ppc);
   uint32_t* own_ctrl = reinterpret_cast<uint32_t*>(p.ep_arena[p.rank] + A.ctrl);
@@ -861,7 +871,7 @@ __global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_
   __syncthreads();
   const int* pair_e = ws_at<const int>(p, L.pair_e);
   for (int i = tid; i < P; i += kDispThreads) {
-    const int d = __ldcg(pair_e + i) / el;
+    const int d = ep_place(p, __ldcg(pair_e + i)) >> 16;
     atomicAdd(&dcount[d], 1);
     if (i < a) atomicAdd(&dbefore[d], 1);
   }
@@ -869,7 +879,7 @@ __global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_
   if (warp == 0) {
     for (int i0 = a; i0 < b; i0 += 32) {
       const int i = i0 + lane;
-      const int d = i < b ? __ldcg(pair_e + i) / el : -1;
+      const int d = i < b ? ep_place(p, __ldcg(pair_e + i)) >> 16 : -1;
       const unsigned m = __match_any_sync(0xffffffffu, d);
       const int rank = d >= 0 ? dbefore[d] + __popc(m & ((1u << lane) - 1u)) : 0;
       __syncwarp();
@@ -882,11 +892,11 @@ __global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_
   for (int j = warp; j < b - a; j += kDispWarps) {
     const int i = a + j, t = i / K;
     const int d = spos[j] >> 24, slot = spos[j] & 0xFFFFFF;
-    const int e = __ldcg(pair_e + i);
+    const int e_local = ep_place(p, __ldcg(pair_e + i)) & 0xFFFF;
     uint8_t* dst_arena = p.ep_arena[d];
     const size_t sidx = static_cast<size_t>(p.rank) * A.slots + slot;
     const int ex = __ldcg(ws_at<const int>(p, L.xexp) + t);
-    if (lane == 0) reinterpret_cast<int2*>(dst_arena + A.rmeta)[sidx] = make_int2(((e - d * el) << 20) | i, ex);
+    if (lane == 0) reinterpret_cast<int2*>(dst_arena + A.rmeta)[sidx] = make_int2((e_local << 20) | i, ex);
     const float sc = exp2i(ex);
     const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
     uint8_t* hi_row = dst_arena + A.stage + sidx * 2 * p.H;
@@ -939,11 +949,15 @@ struct Aux {
   int4 items[kMaxItems];  // (expert or -1, first position, tokens, row block) of the CTA's items
   uint64_t full[8], empty[8];
   uint64_t acc_full[4], acc_empty[4];
+  // up: turn[g] completes when the other epilogue group has released every accumulator of the
+  // item before group g's next one, so no group waits on an accumulator barrier more than one
+  // phase ahead of the MMAs
+  uint64_t turn[2];
   uint64_t mma_done;
   uint32_t tmem;
   int abort;
   int last;  // expert parallel, down: this CTA finished last
-  float amax[2][2][4][32];  // up: [item parity][token half][lane quarter][token] |h| maxima
+  float amax[2][2][2][4][32];  // up: [group][item parity][token half][lane quarter][token] |h| maxima
 };
 
 // Activation box of a tile of n tokens: 2n rows rounded up to 16, 32, 64 or 128 (the MMA's N).
@@ -959,7 +973,7 @@ __device__ __forceinline__ int4 item_desc(const Aux& aux, const int4* tiles, int
 }
 
 template <bool DOWN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(expert_threads(DOWN), 1)
     expert_kernel(const __grid_constant__ Params p, const __grid_constant__ CUtensorMap map_w,
                   const __grid_constant__ CUtensorMap map_sh, const __grid_constant__ CUtensorMap map_b0,
                   const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_b2,
@@ -999,6 +1013,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&aux.acc_full[a], 1);
       mbar_init(&aux.acc_empty[a], kEpiWarps);
     }
+    mbar_init(&aux.turn[0], kEpiWarps);
+    mbar_init(&aux.turn[1], kEpiWarps);
     mbar_init(&aux.mma_done, 1);
     aux.abort = 0;
     fence_mbar_init();
@@ -1081,8 +1097,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // ================================================================ epilogue (warps 2-9)
-    const int q = warp & 3, hf = (warp - 2) >> 2;
+    // ================================================================ epilogue (warps 2-9 [, 10-17])
+    constexpr int kGroups = epi_groups(DOWN);
+    const int grp = (warp - 2) >> 3;  // this warp's group: items grp, grp + kGroups, ...
+    const int q = warp & 3, hf = ((warp - 2) >> 2) & 1;
     const int r = 32 * q + lane;
     if (DOWN) griddep_wait();  // the h blocks' scales come from the up kernel
     // per-item token data, fetched one item ahead: up 2^-e of each token's x split, down the
@@ -1118,28 +1136,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* s2 = shared_tile ? p.sh_s2 : p.s2 + static_cast<size_t>(it.x) * p.s2_stride;
       return s2 + static_cast<size_t>((2 * kRows * it.w + (second ? kRows : 0) + r) / srows) * nkb;
     };
-    int use = 0;
-    int4 it_next = my_items > 0 ? item_desc(aux, tiles, nrb, 0) : make_int4(0, 0, 0, 0);
+    int4 it_next = grp < my_items ? item_desc(aux, tiles, nrb, grp) : make_int4(0, 0, 0, 0);
     float td_next[kMaxI / 128];
     int rm_next = -1;
     float sg_next = 0.f, su_next = 0.f;  // the next item's first-slab scales
-    if (my_items > 0) {
+    if (grp < my_items) {
       token_data(it_next, td_next, rm_next);
       sg_next = __ldg(scale_row(it_next, false));
       su_next = __ldg(scale_row(it_next, true));
     }
-    for (int k = 0; k < my_items; ++k) {
+    for (int k = grp; k < my_items; k += kGroups) {
+      int use = k * nkb;  // accumulator uses run over (item, slab) in the MMA's order
       const int4 it = it_next;
       float td[kMaxI / 128];
 #pragma unroll
       for (int i = 0; i < kMaxI / 128; ++i) td[i] = td_next[i];
       float sg = sg_next, su = su_next;
       const int rm = rm_next;
-      if (k + 1 < my_items) {
-        it_next = item_desc(aux, tiles, nrb, k + 1);
+      if (k + kGroups < my_items) {
+        it_next = item_desc(aux, tiles, nrb, k + kGroups);
         token_data(it_next, td_next, rm_next);
         sg_next = __ldg(scale_row(it_next, false));
         su_next = __ldg(scale_row(it_next, true));
+      }
+      if (kGroups > 1 && k > 0) {
+        // item k's accumulators follow item k - 1's, which the other group reads
+        bool t_ok = true;
+        if (lane == 0) t_ok = wait_or_abort(p, &aux.turn[k & 1], ((k - 1) >> 1) & 1, abort);
+        __syncwarp();
+        (void)t_ok;
       }
       const int nh = min(max(it.z - 32 * hf, 0), 32);  // this warp's tokens of the tile
       const int pbase = it.y + 32 * hf;
@@ -1168,25 +1193,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::fence_after_sync();
           if (nh > 0 && ready) {
             const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
-            float v0[32], v1[32];
-            tc::tmem_ld32(ta, v0);
-            tc::tmem_ld32(ta + 32, v1);
-            tc::tmem_wait_ld();
             if (!DOWN) {
+              // 16 columns (8 tokens' hi / lo) per load keep the two groups within 112 registers
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                a0[j] = fmaf(sg, v0[2 * j] + v0[2 * j + 1], a0[j]);
-                a0[16 + j] = fmaf(sg, v1[2 * j] + v1[2 * j + 1], a0[16 + j]);
+              for (int c = 0; c < 4; ++c) {
+                float v[16];
+                tc::tmem_ld16(ta + 16 * c, v);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a0[8 * c + j] = fmaf(sg, v[2 * j] + v[2 * j + 1], a0[8 * c + j]);
               }
-              tc::tmem_ld32(ta + 128, v0);
-              tc::tmem_ld32(ta + 160, v1);
-              tc::tmem_wait_ld();
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                a1[j] = fmaf(su, v0[2 * j] + v0[2 * j + 1], a1[j]);
-                a1[16 + j] = fmaf(su, v1[2 * j] + v1[2 * j + 1], a1[16 + j]);
+              for (int c = 0; c < 4; ++c) {
+                float v[16];
+                tc::tmem_ld16(ta + 128 + 16 * c, v);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a1[8 * c + j] = fmaf(su, v[2 * j] + v[2 * j + 1], a1[8 * c + j]);
               }
             } else {
+              float v0[32], v1[32];
+              tc::tmem_ld32(ta, v0);
+              tc::tmem_ld32(ta + 32, v1);
+              tc::tmem_wait_ld();
               float hk = td[0];
 #pragma unroll
               for (int i = 1; i < kMaxI / 128; ++i)
@@ -1216,10 +1245,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           su = su_n;
         }
       }
+      if (kGroups > 1) {
+        // every accumulator of item k is released: the other group may start item k + 1
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&aux.turn[(k + 1) & 1]);
+      }
       if (!DOWN) {
         // SwiGLU, h rounded to bf16 (the reference's activation dtype; the shared expert is a chain
         // of bf16 modules), then the per-(token, 128-block) absolute maxima across the 4 quarters
-        const int par = k & 1;
+        const int par = (k / kGroups) & 1;
         const float xi = td[0];
         // branch-free over the 32 tokens: the shared expert's extra bf16 roundings are selects, the
         // tokens past the tile's end are zeroed
@@ -1247,11 +1281,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             a1[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, d));
           }
         }
-        aux.amax[par][hf][q][lane] = a1[0];
-        named_bar(kBarEpi, kEpiThreads);
+        aux.amax[grp][par][hf][q][lane] = a1[0];
+        named_bar(kBarEpi + grp, kEpiThreads);
         float e2[32];
-        const int e_mine = split_exponent(fmaxf(fmaxf(aux.amax[par][hf][0][lane], aux.amax[par][hf][1][lane]),
-                                                fmaxf(aux.amax[par][hf][2][lane], aux.amax[par][hf][3][lane])));
+        const int e_mine =
+            split_exponent(fmaxf(fmaxf(aux.amax[grp][par][hf][0][lane], aux.amax[grp][par][hf][1][lane]),
+                                 fmaxf(aux.amax[grp][par][hf][2][lane], aux.amax[grp][par][hf][3][lane])));
 #pragma unroll
         for (int j = 0; j < 32; ++j) e2[j] = exp2i(__shfl_sync(0xffffffffu, e_mine, j));
         uint8_t* himg = p.ws + L.himg + static_cast<size_t>(2 * pbase) * p.I + kRows * it.w + r;
@@ -1494,10 +1529,12 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream, int phases = 3) {
   const int disp_ctas = (L.cap + pf::pairs_per_cta(L.cap) - 1) / pf::pairs_per_cta(L.cap) +
                         (p.sh_w13 ? (p.T + pf::kDispWarps - 1) / pf::kDispWarps : 0);
   if (pf_launch(pf::dispatch_kernel, dim3(disp_ctas), pf::kDispThreads, 0, stream, "prefill dispatch", p)) return 2;
-  if (pf_launch(pf::expert_kernel<false>, dim3(sms), pf::kThreads, kExpertSmem(false), stream, "prefill up", p, m13,
+  if (pf_launch(pf::expert_kernel<false>, dim3(sms), pf::expert_threads(false), kExpertSmem(false), stream,
+                "prefill up", p, m13,
                 msh13, mb_up[0], mb_up[1], mb_up[2], mb_up[3]))
     return 2;
-  if (pf_launch(pf::expert_kernel<true>, dim3(sms), pf::kThreads, kExpertSmem(true), stream, "prefill down", p, m2,
+  if (pf_launch(pf::expert_kernel<true>, dim3(sms), pf::expert_threads(true), kExpertSmem(true), stream,
+                "prefill down", p, m2,
                 msh2, mb_dn[0], mb_dn[1], mb_dn[2], mb_dn[3]))
     return 2;
   const int c_threads = p.T * (H / 8);
@@ -1760,8 +1797,8 @@ static int prefill_ep(int phases, const void* x, int T, int H, int I, const void
                       int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride,
                       int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
                       int sh_srows, const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out,
-                      void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
-                      size_t workspace_bytes, void* stream) {
+                      void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas, const int* owner,
+                      void* workspace, size_t workspace_bytes, void* stream) {
   dm3::note_launches(0);
   int rc = check_ep(world, rank, T, tokens_per_rank, n_router, arenas);
   if (rc) return rc;
@@ -1796,6 +1833,7 @@ static int prefill_ep(int phases, const void* x, int T, int H, int I, const void
   p.ids_out = ids_out;
   p.w_out = static_cast<__nv_bfloat16*>(w_out);
   set_ep(p, world, rank, tokens_per_rank, arenas);
+  p.ep_owner = owner;
   return dm3::launch_prefill(p, static_cast<cudaStream_t>(stream), phases);
 }
 
@@ -1805,18 +1843,18 @@ extern "C" int dm3_moe_prefill_ep(const void* x, int T, int H, int I, const void
                                   const float* s2, int64_t s2_stride, int srows, const void* sh_w13,
                                   const float* sh_s13, const void* sh_w2, const float* sh_s2, int sh_srows,
                                   const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
-                                  int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+                                  int world, int rank, int tokens_per_rank, void* const* arenas, const int* owner,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
   return prefill_ep(3, x, T, H, I, router_w, n_router, top_k, logits_bf16, logit_bias, w13, w13_stride, s13,
                     s13_stride, w2, w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows, sh_gate,
-                    out_bias, y, ids_out, w_out, world, rank, tokens_per_rank, arenas, workspace, workspace_bytes,
-                    stream);
+                    out_bias, y, ids_out, w_out, world, rank, tokens_per_rank, arenas, owner, workspace,
+                    workspace_bytes, stream);
 }
 
 extern "C" int dm3_ep_dispatch(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
                                int logits_bf16, const float* logit_bias, const void* sh_gate, int64_t* ids_out,
                                void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas,
-                               void* workspace, size_t workspace_bytes, void* stream) {
+                               const int* owner, void* workspace, size_t workspace_bytes, void* stream) {
   // the expert operands are not read by this phase: the router weight stands in for them in the
   // argument checks (and, when the shared gate is given, for the shared expert's presence)
   return prefill_ep(1, x, T, H, I, router_w, n_router, top_k, logits_bf16, logit_bias, router_w, 2LL * I * H,
@@ -1824,7 +1862,7 @@ extern "C" int dm3_ep_dispatch(const void* x, int T, int H, int I, const void* r
                     reinterpret_cast<const float*>(router_w), 0, 128, sh_gate ? router_w : nullptr,
                     reinterpret_cast<const float*>(router_w), router_w, reinterpret_cast<const float*>(router_w), 128,
                     sh_gate, nullptr, const_cast<void*>(x), ids_out, w_out, world, rank, tokens_per_rank, arenas,
-                    workspace, workspace_bytes, stream);
+                    owner, workspace, workspace_bytes, stream);
 }
 
 extern "C" int dm3_ep_combine(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
@@ -1836,5 +1874,5 @@ extern "C" int dm3_ep_combine(const void* x, int T, int H, int I, const void* ro
                               void* stream) {
   return prefill_ep(2, x, T, H, I, router_w, n_router, top_k, 1, nullptr, w13, w13_stride, s13, s13_stride, w2,
                     w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows, sh_gate, out_bias, y,
-                    nullptr, nullptr, world, rank, tokens_per_rank, arenas, workspace, workspace_bytes, stream);
+                    nullptr, nullptr, world, rank, tokens_per_rank, arenas, nullptr, workspace, workspace_bytes, stream);
 }

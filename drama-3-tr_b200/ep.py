@@ -35,6 +35,34 @@ def _arena_array(arenas: List[int]):
     return arr
 
 
+def balanced_placement(load: Tensor, world: int) -> Tensor:
+    """A placement of E experts over `world` ranks, E / world each, that evens out the expected
+    load: experts by descending load, each to the rank with the least load among those with room
+    (greedy longest-processing-time). Returns int32 [E] of (rank << 16) | local index, local
+    indices in ascending expert order on each rank."""
+    E = load.numel()
+    el = E // world
+    order = torch.argsort(load.double().cpu(), descending=True, stable=True).tolist()
+    tot = [0.0] * world
+    members: list = [[] for _ in range(world)]
+    for e in order:
+        r = min((r for r in range(world) if len(members[r]) < el), key=lambda r: (tot[r], r))
+        members[r].append(e)
+        tot[r] += float(load[e])
+    owner = torch.empty(E, dtype=torch.int32)
+    for r in range(world):
+        for i, e in enumerate(sorted(members[r])):
+            owner[e] = (r << 16) | i
+    return owner
+
+
+def local_experts(owner: Tensor, rank: int) -> Tensor:
+    """The global ids of `rank`'s experts in local index order under a placement."""
+    o = owner.cpu().long()
+    mine = torch.nonzero((o >> 16) == rank).flatten()
+    return mine[torch.argsort(o[mine] & 0xFFFF)]
+
+
 def ep_workspace(device: torch.device, nbytes: int) -> Tensor:
     """The expert-parallel scratch of this rank (grown on demand, zero-initialised)."""
     key = device.index if device.index is not None else torch.cuda.current_device()
@@ -103,11 +131,22 @@ class ExpertParallel:
     def moe_prefill(self, x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, logit_bias: Optional[Tensor],
                     w13: Tensor, s13: Tensor, w2: Tensor, s2: Tensor, sh_w13: Optional[Tensor] = None,
                     sh_s13: Optional[Tensor] = None, sh_w2: Optional[Tensor] = None, sh_s2: Optional[Tensor] = None,
-                    sh_gate: Optional[Tensor] = None, out_bias: Optional[Tensor] = None):
+                    sh_gate: Optional[Tensor] = None, out_bias: Optional[Tensor] = None,
+                    owner: Optional[Tensor] = None):
         """This rank's part of the prefill layer: x [T, H] its tokens, w13 / s13 / w2 / s2 its
-        E / world experts. Returns (y [T, H], ids [T, k], routing weights [T, k])."""
+        E / world experts (contiguous blocks, or as `owner` places them). Returns (y [T, H],
+        ids [T, k], routing weights [T, k])."""
         return moe_prefill_ep(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2,
-                              sh_s2, sh_gate, out_bias, self.world, self.rank, self.tokens_per_rank, self.arenas)
+                              sh_s2, sh_gate, out_bias, self.world, self.rank, self.tokens_per_rank, self.arenas,
+                              owner)
+
+
+def _owner(owner: Optional[Tensor], E: int) -> Optional[Tensor]:
+    if owner is None:
+        return None
+    if owner.numel() != E or not owner.is_cuda:
+        raise RuntimeError("owner must be an int32 [E] device tensor")
+    return owner.to(torch.int32).contiguous()
 
 
 def _ep_checks(x: Tensor, router_w: Tensor, world: int, E_local: int):
@@ -122,10 +161,10 @@ def moe_prefill_ep(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, l
                    w13: Tensor, s13: Tensor, w2: Tensor, s2: Tensor, sh_w13: Optional[Tensor], sh_s13: Optional[Tensor],
                    sh_w2: Optional[Tensor], sh_s2: Optional[Tensor], sh_gate: Optional[Tensor],
                    out_bias: Optional[Tensor], world: int, rank: int, tokens_per_rank: int,
-                   arenas: List[int]) -> tuple[Tensor, Tensor, Tensor]:
+                   arenas: List[int], owner: Optional[Tensor] = None) -> tuple[Tensor, Tensor, Tensor]:
     """Expert-parallel prefill layer (routing, NVLink dispatch, local experts, NVLink return,
     combine) for this rank's tokens."""
-    _require_cuda(x, router_w, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias)
+    _require_cuda(x, router_w, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias, owner)
     lib = _lib.load()
     w13, w2 = _fp8_bytes(w13), _fp8_bytes(w2)
     x = x.contiguous()
@@ -134,6 +173,7 @@ def moe_prefill_ep(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, l
     _ep_checks(x, router_w, world, El)
     E = router_w.shape[0]
     router_w = router_w.contiguous()
+    owner = _owner(owner, E)
     if logit_bias is not None:
         logit_bias = logit_bias.float().contiguous()
     sh_w13, sh_s13, sh_w2, sh_s2, sh_srows = _shared_args(sh_w13, sh_s13, sh_w2, sh_s2, H, I)
@@ -150,14 +190,14 @@ def moe_prefill_ep(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, l
                                 _ptr(logit_bias), _ptr(w13), w13s, _ptr(s13), s13s, _ptr(w2), w2s, _ptr(s2), s2s,
                                 srows, _ptr(sh_w13), _ptr(sh_s13), _ptr(sh_w2), _ptr(sh_s2), sh_srows, _ptr(sh_gate),
                                 _ptr(out_bias), _ptr(y), _ptr(ids), _ptr(wts), world, rank, tokens_per_rank,
-                                _arena_array(arenas), _ptr(ws), ws.numel(), _stream(dev))
+                                _arena_array(arenas), _ptr(owner), _ptr(ws), ws.numel(), _stream(dev))
     _lib.check(rc, "dm3_moe_prefill_ep")
     return y, ids, wts
 
 
 @moe_prefill_ep.register_fake
 def _(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias,
-      world, rank, tokens_per_rank, arenas):
+      world, rank, tokens_per_rank, arenas, owner=None):
     T = x.shape[0]
     return (torch.empty_like(x, dtype=BF16), x.new_empty((T, top_k), dtype=torch.int64),
             x.new_empty((T, top_k), dtype=BF16))
@@ -166,7 +206,7 @@ def _(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_
 @torch.library.custom_op("dm3::ep_dispatch", mutates_args=())
 def ep_dispatch(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, logit_bias: Optional[Tensor],
                 sh_gate: Optional[Tensor], intermediate: int, world: int, rank: int, tokens_per_rank: int,
-                arenas: List[int]) -> tuple[Tensor, Tensor]:
+                arenas: List[int], owner: Optional[Tensor] = None) -> tuple[Tensor, Tensor]:
     """First half of the expert-parallel layer: routes this rank's tokens and sends every (token, k)
     pair to the rank owning its expert. Returns (ids [T, k], routing weights [T, k]); the pairs'
     state stays in this rank's workspace and the owners' arenas for ep_combine."""
@@ -182,19 +222,21 @@ def ep_dispatch(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, logi
         logit_bias = logit_bias.float().contiguous()
     if sh_gate is not None:
         sh_gate = sh_gate.to(BF16).reshape(-1).contiguous()
+    owner = _owner(owner, E)
     ids = torch.empty((T, top_k), dtype=torch.int64, device=x.device)
     wts = torch.empty((T, top_k), dtype=BF16, device=x.device)
     ws = ep_workspace(x.device, lib.dm3_moe_prefill_ep_workspace_bytes(world, tokens_per_rank, H, intermediate, E,
                                                                          top_k))
     rc = lib.dm3_ep_dispatch(_ptr(x), T, H, intermediate, _ptr(router_w), E, top_k, 1 if logits_bf16 else 0,
                              _ptr(logit_bias), _ptr(sh_gate), _ptr(ids), _ptr(wts), world, rank, tokens_per_rank,
-                             _arena_array(arenas), _ptr(ws), ws.numel(), _stream(x.device))
+                             _arena_array(arenas), _ptr(owner), _ptr(ws), ws.numel(), _stream(x.device))
     _lib.check(rc, "dm3_ep_dispatch")
     return ids, wts
 
 
 @ep_dispatch.register_fake
-def _(x, router_w, top_k, logits_bf16, logit_bias, sh_gate, intermediate, world, rank, tokens_per_rank, arenas):
+def _(x, router_w, top_k, logits_bf16, logit_bias, sh_gate, intermediate, world, rank, tokens_per_rank, arenas,
+      owner=None):
     T = x.shape[0]
     return x.new_empty((T, top_k), dtype=torch.int64), x.new_empty((T, top_k), dtype=BF16)
 

@@ -238,15 +238,18 @@ size_t dm3_moe_prefill_ep_workspace_bytes(int world, int tokens_per_rank, int H,
  * The prefill layer of dm3_moe_prefill under expert parallelism: x, y, ids_out, w_out are this
  * rank's T tokens; w13 / s13 / w2 / s2 hold this rank's n_router / world experts (local index
  * order); the router weight, logit bias and shared expert are replicated. The result equals
- * dm3_moe_prefill on the concatenated tokens.
+ * dm3_moe_prefill on the concatenated tokens. owner: optional int32 [n_router] on the device,
+ * (rank << 16) | local index of every expert, for a placement other than contiguous blocks (it
+ * must give every rank n_router / world experts, and each rank's w13 / w2 must follow it); null
+ * places expert e on rank e / (n_router / world).
  */
 int dm3_moe_prefill_ep(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
                        int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride, const float* s13,
                        int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2, int64_t s2_stride,
                        int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
                        int sh_srows, const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
-                       int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
-                       size_t workspace_bytes, void* stream);
+                       int world, int rank, int tokens_per_rank, void* const* arenas, const int* owner,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * The two halves of dm3_moe_prefill_ep. dm3_ep_dispatch routes this rank's tokens and sends every
@@ -254,10 +257,11 @@ int dm3_moe_prefill_ep(const void* x, int T, int H, int I, const void* router_w,
  * the pairs every rank sent here into expert tiles, runs this rank's experts, sends each output row
  * back to its source rank, and combines this rank's tokens (+ shared expert, + bias). Call them in
  * this order on the same stream with the same workspace; sh_gate must be given to both or neither.
+ * owner as dm3_moe_prefill_ep (dm3_ep_combine takes this rank's experts in that placement).
  */
 int dm3_ep_dispatch(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
                     int logits_bf16, const float* logit_bias, const void* sh_gate, int64_t* ids_out, void* w_out,
-                    int world, int rank, int tokens_per_rank, void* const* arenas, void* workspace,
+                    int world, int rank, int tokens_per_rank, void* const* arenas, const int* owner, void* workspace,
                     size_t workspace_bytes, void* stream);
 int dm3_ep_combine(const void* x, int T, int H, int I, const void* router_w, int n_router, int top_k,
                    const void* w13, int64_t w13_stride, const float* s13, int64_t s13_stride, const void* w2,

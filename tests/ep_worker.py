@@ -98,6 +98,14 @@ def gpu_rank(rank: int, world: int, store: str, out_dir: str) -> None:
             graph.replay()
         torch.cuda.synchronize()
         res["graph_y"] = bool(torch.equal(gy, ref_y[sl]))
+        # a load-balanced placement: this rank holds the experts the table gives it, in local order
+        owner = dm3.ep.balanced_placement(torch.exp(bias.float().cpu()), world)
+        mine = dm3.ep.local_experts(owner, rank).to(dev)
+        lw_b = (w13[mine], s13[mine], w2[mine], s2[mine])
+        yb, idsb, _ = grp.moe_prefill(xs, gate, K, True, bias, *lw_b, sh13, shs13, sh2, shs2, shg, None,
+                                      owner=owner.to(dev))
+        torch.cuda.synchronize()
+        res["placed_y"] = bool(torch.equal(yb, ref_y[sl])) and bool(torch.equal(idsb, ref_ids[sl]))
         ws = dm3.ep._ep_workspaces[rank]
         res["status"] = dm3.ops.moe_status(ws)
         del graph

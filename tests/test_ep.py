@@ -46,3 +46,4 @@ def test_ep_prefill_two_gpus(tmp_path):
         assert r["fused_y"], r
         assert r["split_y0"] and r["split_y1"], r
         assert r["graph_y"], r
+        assert r["placed_y"], r
