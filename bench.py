@@ -199,8 +199,127 @@ def time_cpu_port(layers_cpu, budget_s: float):
     return reps / el, reps, torch.get_num_threads()
 
 
+def run_decode_sharded(args, world, rank, local):
+    """One 2-row frame of 40 layers sharded over `world` GPUs: every rank the same rows, router and
+    routing, its 256 / world experts per layer (rank 0 the shared expert), and an NVLink all-reduce
+    of the partial sums inside each layer's combine kernel."""
+    import drama3_b200 as dm3
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local)
+    n_layers = args.layers
+    el = E // world
+    layers = []
+    for l in range(n_layers):
+        seed = 1000 + l
+        g = torch.Generator(device=dev).manual_seed(seed)  # replicated parts: same on every rank
+        L = {"gate": (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)}
+        L["sh_w13"], L["sh_s13"] = dm3.fp8_block(torch.randn(2 * I, H, generator=g, device=dev) * 0.02)
+        L["sh_w2"], L["sh_s2"] = dm3.fp8_block(torch.randn(H, I, generator=g, device=dev) * 0.02)
+        L["sh_gate"] = (torch.randn(H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        L["x"] = rms(torch.randn(T, H, generator=g, device=dev)).to(torch.bfloat16)
+        gl = torch.Generator(device=dev).manual_seed(seed * 100 + rank)  # this rank's experts
+        L["w13"], L["s13"] = dm3.fp8_block(torch.randn(el, 2 * I, H, generator=gl, device=dev) * 0.02)
+        L["w2"], L["s2"] = dm3.fp8_block(torch.randn(el, H, I, generator=gl, device=dev) * 0.02)
+        layers.append(L)
+    grp = dm3.ep.ExpertParallel(PF_T // world, H, TOPK)
+
+    def call(L, x):
+        return grp.moe_layer(x, L["gate"], TOPK, True, None, L["w13"], L["s13"], L["w2"], L["s2"], L["sh_w13"],
+                             L["sh_s13"], L["sh_w2"], L["sh_s2"], L["sh_gate"], None)
+
+    outs = [call(L, L["x"]) for L in layers]
+    torch.cuda.synchronize()
+    barrier(world)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        gouts = [call(L, L["x"]) for L in layers]
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert dm3.ops.moe_status(dm3.ops.moe_workspace(dev, H, I)) == 0, "device status word set during warm-up"
+    for o, g2 in zip(outs, gouts):
+        assert torch.equal(o[1], g2[1]), "graph replay routed differently from eager"
+    # this rank's HBM bytes per frame: its selected experts, the router, the shared expert on rank 0
+    bytes_rank = 0
+    for L, o in zip(layers, outs):
+        ids = o[1]
+        mine = torch.unique(ids[(ids // el) == rank])
+        bytes_rank += int(mine.numel()) * EXPERT_BYTES + E * H * 2 + 2 * T * H * 2
+        if rank == 0:
+            bytes_rank += EXPERT_BYTES + H * 2
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    launches = args.steps * n_layers * dm3._lib.load().dm3_last_launch_count()
+    xs_host = torch.stack([L["x"].cpu() for L in layers]).pin_memory()
+    y_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xs_dev = torch.stack([L["x"] for L in layers])
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        g2outs = [call(L, xs_dev[l])[0] for l, L in enumerate(layers)]
+
+    def e2e_step():
+        xs_dev.copy_(xs_host, non_blocking=True)
+        g2.replay()
+        y_host.copy_(g2outs[-1], non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+    bt = torch.tensor([float(bytes_rank)], device=dev)
+    dist.all_reduce(bt, op=dist.ReduceOp.MAX)
+    pk = peaks()
+    achieved = float(bt.item()) / (ms * 1e-3) / 1e9
+    clk_sum = clk.summary()
+    del graph, g2
+    grp.close()
+    return {
+        "metric": METRIC, "value": round(n_layers * 1000.0 / ms, 1), "unit": "layer-frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "us_per_layer": round(ms * 1000.0 / n_layers, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "e4m3 weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,0.02) weights, RMS-normalised N(0,1) rows)",
+        "config": {"workload": "decode_fp8_256x40", "layers": n_layers, "rows": T, "hidden": H, "intermediate": I,
+                   "experts": E, "top_k": TOPK, "router": "bf16, logits rounded to bf16",
+                   "shared_expert": "block-FP8 128x128 + bf16 sigmoid gate (rank 0)", "scales": "128x128 fp32",
+                   "cuda_graph": True,
+                   "parallelism": f"sharded x{world}: {el} experts per rank, NVLink all-reduce in the combine kernel"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": f"{pk['source']} HBM copy bandwidth",
+                     "kernel": "one sharded decode frame per GPU (the busiest rank's HBM bytes / frame time)",
+                     "bytes_per_launch": round(float(bt.item()) / n_layers), "traffic": None},
+        "gpu_launches": launches,
+        "e2e": {"value": round(n_layers * 1000.0 / ms_e2e, 1), "unit": "layer-frames/s",
+                "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(y_host.numel() * 2),
+                "ms_per_step": round(ms_e2e, 4),
+                "path": "pinned host rows -> H2D -> captured ExpertParallel.moe_layer x 40 -> D2H of the last layer"},
+        "clocks": {k: clk_sum[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+    }
+
+
 def run_decode(args, world, rank, local, speaker=False):
     import drama3_b200 as dm3
+
+    if world > 1 and args.decode_mode == "sharded" and not speaker:
+        return run_decode_sharded(args, world, rank, local)
 
     dev = torch.device("cuda", local)
     n_layers = args.layers
@@ -725,6 +844,8 @@ def main():
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-mode", default="replicas", choices=["replicas", "sharded"],
+                    help="n_gpus > 1 decode: independent replicas (weak scaling) or one frame sharded (strong)")
     ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement of the expert-parallel prefill (n_gpus > 1)")
     args = ap.parse_args()

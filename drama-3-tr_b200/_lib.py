@@ -53,6 +53,8 @@ SIGNATURES = {
     "dm3_ep_dispatch": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p, _sz, _p]),
     "dm3_ep_combine": (_i, [_p, _i, _i, _i, _p, _i, _i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p, _p, _p,
                             _i, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
+    "dm3_moe_layer_ep": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p,
+                              _p, _p, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
     "dm3_last_launch_count": (_i, []),
 }
 

@@ -34,6 +34,7 @@
 #include <utility>
 
 #include "dm3_common.cuh"
+#include "dm3_ep.cuh"
 #include "dm3_internal.h"
 #include "dm3_route.cuh"
 #include "dm3_tc.cuh"
@@ -93,6 +94,12 @@ struct Params {
   const float* out_bias;
   __nv_bfloat16* y;
   uint8_t* ws;
+  int sh_slot;  // slot 0 is the shared expert on this rank (the layer has one; rank 0 when sharded)
+  // sharded over `world` ranks (world > 1): this rank runs the experts [rank * ep_el, +ep_el) of
+  // the routing every rank computes alike, whose weights w13 / w2 hold; the partial sums meet in an
+  // all-reduce over the expert-parallel arenas (ep_arena[r] = rank r's, mapped here)
+  int world, rank, ep_tl, ep_el;
+  uint8_t* ep_arena[8];
 };
 
 
@@ -102,7 +109,7 @@ struct Params {
 // serves every T of a given (H, I). Nothing in it carries state from one call to the next except
 // the sticky status word (the route kernel's CTA counter is back at zero after every call).
 struct WsLayout {
-  size_t ctrl, slot_expert, coef, logits, himg, himg_stride, hinv, ximg, xinv, partial, total;
+  size_t ctrl, slot_expert, coef, gate, logits, himg, himg_stride, hinv, ximg, xinv, partial, total;
 };
 enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
 
@@ -117,6 +124,8 @@ __host__ __device__ inline WsLayout ws_layout(int H, int I) {
   o += align_up(kMaxSlots * 4, 16);
   L.coef = o;
   o += align_up(kMaxSlots * kMaxT * 4, 16);
+  L.gate = o;  // [kMaxT] the shared expert's sigmoid gate per row
+  o += align_up(kMaxT * 4, 16);
   L.logits = o;
   o += align_up(kMaxT * (kMaxRouter + 1) * 4, 16);
   // per slot: h split into e4m3 hi (rows 0-3) and lo (rows 4-7) as the down kernel's activation
@@ -203,7 +212,7 @@ struct ExpertRef {
 
 __device__ __forceinline__ ExpertRef expert_ref(const Params& p, int slot, const int* tab_expert) {
   ExpertRef r;
-  if (slot == 0 && p.sh_w13 != nullptr) {
+  if (slot == 0 && p.sh_slot) {
     r.w13 = p.sh_w13;
     r.s13 = p.sh_s13;
     r.w2 = p.sh_w2;
@@ -423,29 +432,32 @@ __device__ void write_table(const Params& p, const WsLayout& L, RouteTail& rt, i
   const bool valid = lane < n;
   const int e = valid ? rt.sel_e[lane] : 0;
   const int t = valid ? lane / p.top_k : 0;
+  // sharded: only the experts this rank holds get slots, numbered by their local index
+  const bool own = valid && (p.world <= 1 || e / p.ep_el == p.rank);
   if (lane < kMaxRouter / 32) rt.bitmap[lane] = 0u;
   __syncwarp();
-  if (valid) atomicOr(&rt.bitmap[e >> 5], 1u << (e & 31));
+  if (own) atomicOr(&rt.bitmap[e >> 5], 1u << (e & 31));
   __syncwarp();
-  int rank = 0, total = 0;
+  int srank = 0, total = 0;
 #pragma unroll
   for (int w = 0; w < kMaxRouter / 32; ++w) {
     const uint32_t word = rt.bitmap[w];
     total += __popc(word);
-    if (w < (e >> 5)) rank += __popc(word);
+    if (w < (e >> 5)) srank += __popc(word);
   }
-  rank += __popc(rt.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
-  const bool sh = p.sh_w13 != nullptr;
+  srank += __popc(rt.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
+  const bool sh = p.sh_slot != 0;
   const int base = sh ? 1 : 0;
   int* gse = reinterpret_cast<int*>(p.ws + L.slot_expert);
   float* gco = reinterpret_cast<float*>(p.ws + L.coef);
   for (int i = lane; i < kMaxSlots * kMaxT; i += 32) gco[i] = 0.f;
   __syncwarp();
-  if (valid) {
-    gse[base + rank] = e;  // rows that chose the same expert write the same value
-    gco[(base + rank) * kMaxT + t] = rt.sel_w[lane];
+  if (own) {
+    gse[base + srank] = p.world > 1 ? e - p.rank * p.ep_el : e;  // rows that chose the same expert write the same value
+    gco[(base + srank) * kMaxT + t] = rt.sel_w[lane];
   }
   if (sh && lane < p.T) gco[lane] = rt.shared_coef[lane];
+  if (lane < p.T) reinterpret_cast<float*>(p.ws + L.gate)[lane] = rt.shared_coef[lane];
   if (sh && lane == 0) gse[0] = -1;
   if (lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(base + total);
 }
@@ -743,7 +755,7 @@ __device__ void epilogue_up(const Params& p, const WsLayout& L, Aux& aux, uint32
     for (int t = 0; t < kMaxT; ++t) aux.upv[r - kUpHalf][t] = acc[t] * aux.xinv[t];
   named_bar(kBarEpi, kEpiThreads);
   if (r >= kUpHalf) return;
-  const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
+  const bool shared_slot = slot == 0 && p.sh_slot;
   float hb[kMaxT];
   uint32_t am[kMaxT];
 #pragma unroll
@@ -812,7 +824,7 @@ __device__ void epilogue_down(const Params& p, const WsLayout& L, Aux& aux, uint
   tc::fence_before_sync();
   __syncwarp();
   if (lane == 0) mbar_arrive(acc_empty);
-  const bool shared_slot = slot == 0 && p.sh_w13 != nullptr;
+  const bool shared_slot = slot == 0 && p.sh_slot;
   float* part = partial_block(p, L, nb, slot);
   for (int t = 0; t < p.T; ++t)
     __stcg(part + t * kBlockRows + r, acc[t] * (shared_slot ? 1.f : aux.tab.coef[slot * kMaxT + t]));
@@ -839,7 +851,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   Aux& aux = *reinterpret_cast<Aux*>(smem + S.aux);
   Table& tab = aux.tab;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool sh = p.sh_w13 != nullptr;
+  const bool sh = p.sh_slot != 0;
   const int per_slot = DOWN ? p.H / kBlockRows : p.I / kUpHalf;
   const int nkb = (DOWN ? p.I : p.H) / 128;  // 128-wide k blocks (slabs) per item
   const int nchunks = (nkb + 1) / 2;         // ring stages per item
@@ -1121,23 +1133,72 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
   if (active && p.out_bias) bias = __ldg(p.out_bias + n);
   griddep_wait();
   griddep_launch();
+  const bool sh = p.sh_w13 != nullptr;  // the layer has a shared expert (computed where sh_slot)
+  float R = 0.f, S = 0.f;               // routed sum, raw shared-expert output
+  if (active) {
+    // the slot count and every slot's partial are requested at once: one L2 round trip; slots past
+    // the count hold stale data and are masked
+    const int nb = n / kBlockRows, r = n % kBlockRows;
+    const float* col = partial_block(p, L, nb, 0) + t * kBlockRows + r;
+    const uint32_t n_slots = __ldcg(ctrl(p, L) + CTRL_NSLOTS);
+    float v[kMaxSlots];
+#pragma unroll
+    for (int s = 0; s < kMaxSlots; ++s) v[s] = __ldcg(col + s * kMaxT * kBlockRows);
+    R = (!p.sh_slot && n_slots > 0u) ? v[0] : 0.f;
+#pragma unroll
+    for (int s = 1; s < kMaxSlots; ++s) R += static_cast<uint32_t>(s) < n_slots ? v[s] : 0.f;
+    S = (p.sh_slot && n_slots > 0u) ? v[0] : 0.f;
+  }
+  if (p.world > 1) {
+    // one-shot all-reduce over NVLink: every rank stores its two partials into every rank's arena
+    // (region of the call's epoch parity), the last CTA raises this rank's flag on every rank, and
+    // each CTA sums the ranks' partials in rank order once every flag holds the epoch
+    __shared__ int s_last;
+    const ep::EpLayout A = ep::ep_layout(p.world, p.ep_tl, p.top_k, p.H);
+    uint32_t* own_ctrl = reinterpret_cast<uint32_t*>(p.ep_arena[p.rank] + A.ctrl);
+    const uint32_t epoch = __ldcg(own_ctrl + ep::EP_RED_EPOCH) + 1u;
+    const size_t region = static_cast<size_t>(epoch & 1u) * p.world * 2 * kMaxT * p.H;
+    if (active)
+      for (int d = 0; d < p.world; ++d) {
+        float* red = reinterpret_cast<float*>(p.ep_arena[d] + A.red) + region;
+        __stcg(red + (static_cast<size_t>(p.rank * 2 + 0) * kMaxT + t) * p.H + n, R);
+        __stcg(red + (static_cast<size_t>(p.rank * 2 + 1) * kMaxT + t) * p.H + n, S);
+      }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // cumulative over the CTA's stores, ordered by the barrier above
+      s_last = atomicAdd(own_ctrl + ep::EP_RED_COUNT, 1u) == gridDim.x - 1 ? 1 : 0;
+    }
+    __syncthreads();
+    if (s_last) {
+      if (threadIdx.x < p.world) {
+        __threadfence_system();
+        ep::st_release_sys(reinterpret_cast<uint32_t*>(p.ep_arena[threadIdx.x] + A.redflag) + p.rank, epoch);
+      }
+      if (threadIdx.x == 0) {
+        own_ctrl[ep::EP_RED_COUNT] = 0u;
+        own_ctrl[ep::EP_RED_EPOCH] = epoch;
+      }
+    }
+    if (threadIdx.x < p.world &&
+        !ep::wait_epoch(reinterpret_cast<const uint32_t*>(p.ep_arena[p.rank] + A.redflag) + threadIdx.x, epoch))
+      flag_error(p, L, STATUS_TIMEOUT);
+    __syncthreads();
+    if (active) {
+      const float* red = reinterpret_cast<const float*>(p.ep_arena[p.rank] + A.red) + region;
+      R = 0.f;
+      S = 0.f;
+      for (int s = 0; s < p.world; ++s) {
+        R += __ldcg(red + (static_cast<size_t>(s * 2 + 0) * kMaxT + t) * p.H + n);
+        S += __ldcg(red + (static_cast<size_t>(s * 2 + 1) * kMaxT + t) * p.H + n);
+      }
+    }
+  }
   if (!active) return;
-  const bool sh = p.sh_w13 != nullptr;
-  // the slot count, the shared gate and every slot's partial are requested at once: one L2 round
-  // trip; slots past the count hold stale data and are masked
-  const int nb = n / kBlockRows, r = n % kBlockRows;
-  const float* col = partial_block(p, L, nb, 0) + t * kBlockRows + r;
-  const uint32_t n_slots = __ldcg(ctrl(p, L) + CTRL_NSLOTS);
-  const float gate = sh ? __ldcg(reinterpret_cast<const float*>(p.ws + L.coef) + t) : 0.f;
-  float v[kMaxSlots];
-#pragma unroll
-  for (int s = 0; s < kMaxSlots; ++s) v[s] = __ldcg(col + s * kMaxT * kBlockRows);
-  float acc = (!sh && n_slots > 0u) ? v[0] : 0.f;
-#pragma unroll
-  for (int s = 1; s < kMaxSlots; ++s) acc += static_cast<uint32_t>(s) < n_slots ? v[s] : 0.f;
-  acc = bf16_round(acc);
+  const float gate = sh ? __ldcg(reinterpret_cast<const float*>(p.ws + L.gate) + t) : 0.f;
+  float acc = bf16_round(R);
   if (p.out_bias) acc = bf16_round(acc + bias);
-  if (sh) acc += bf16_round(gate * bf16_round(v[0]));
+  if (sh) acc += bf16_round(gate * bf16_round(S));
   p.y[static_cast<size_t>(t) * p.H + n] = __float2bfloat16_rn(acc);
 }
 
@@ -1315,13 +1376,13 @@ extern "C" int dm3_moe_forward(const void* x, int T, int H, int I, const int64_t
   return dm3::launch_moe(p, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int dm3_moe_layer(const void* x, int T, int H, int I, const void* router_w, int router_dtype,
-                             int n_router, int top_k, int logits_bf16, const float* logit_bias, const void* w13,
-                             int64_t w13_stride, const float* s13, int64_t s13_stride, const void* w2,
-                             int64_t w2_stride, const float* s2, int64_t s2_stride, int srows, const void* sh_w13,
-                             const float* sh_s13, const void* sh_w2, const float* sh_s2, int sh_srows,
-                             const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
-                             void* workspace, size_t workspace_bytes, void* stream) {
+static int moe_layer_impl(const void* x, int T, int H, int I, const void* router_w, int router_dtype, int n_router,
+                          int top_k, int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
+                          const float* s13, int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2,
+                          int64_t s2_stride, int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2,
+                          const float* sh_s2, int sh_srows, const void* sh_gate, const float* out_bias, void* y,
+                          int64_t* ids_out, void* w_out, void* workspace, size_t workspace_bytes, void* stream,
+                          int world, int rank, int tokens_per_rank, void* const* arenas) {
   dm3::note_launches(0);
   int rc = check_common(T, H, I, top_k, x, w13, w13_stride, s13, w2, w2_stride, s2, srows, y, workspace,
                         workspace_bytes);
@@ -1370,7 +1431,47 @@ extern "C" int dm3_moe_layer(const void* x, int T, int H, int I, const void* rou
   p.out_bias = out_bias;
   p.y = static_cast<__nv_bfloat16*>(y);
   p.ws = static_cast<uint8_t*>(workspace);
+  p.sh_slot = sh_w13 != nullptr && (world <= 1 || rank == 0) ? 1 : 0;
+  if (world > 1) {
+    if (world > 8 || rank < 0 || rank >= world || n_router % world || !arenas || tokens_per_rank < 1)
+      return dm3::set_error("bad expert-parallel arguments (world in [2, 8], rank, n_router % world, arenas)"), 1;
+    for (int r = 0; r < world; ++r)
+      if (!arenas[r]) return dm3::set_error("null arena pointer"), 1;
+    p.world = world;
+    p.rank = rank;
+    p.ep_tl = tokens_per_rank;
+    p.ep_el = n_router / world;
+    p.n_experts = p.ep_el;  // w13 / w2 hold this rank's experts
+    for (int r = 0; r < 8; ++r) p.ep_arena[r] = r < world ? static_cast<uint8_t*>(arenas[r]) : nullptr;
+  }
   return dm3::launch_moe(p, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dm3_moe_layer(const void* x, int T, int H, int I, const void* router_w, int router_dtype,
+                             int n_router, int top_k, int logits_bf16, const float* logit_bias, const void* w13,
+                             int64_t w13_stride, const float* s13, int64_t s13_stride, const void* w2,
+                             int64_t w2_stride, const float* s2, int64_t s2_stride, int srows, const void* sh_w13,
+                             const float* sh_s13, const void* sh_w2, const float* sh_s2, int sh_srows,
+                             const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out, void* w_out,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  return moe_layer_impl(x, T, H, I, router_w, router_dtype, n_router, top_k, logits_bf16, logit_bias, w13, w13_stride,
+                        s13, s13_stride, w2, w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows,
+                        sh_gate, out_bias, y, ids_out, w_out, workspace, workspace_bytes, stream, 1, 0, 0, nullptr);
+}
+
+extern "C" int dm3_moe_layer_ep(const void* x, int T, int H, int I, const void* router_w, int router_dtype,
+                                int n_router, int top_k, int logits_bf16, const float* logit_bias, const void* w13,
+                                int64_t w13_stride, const float* s13, int64_t s13_stride, const void* w2,
+                                int64_t w2_stride, const float* s2, int64_t s2_stride, int srows,
+                                const void* sh_w13, const float* sh_s13, const void* sh_w2, const float* sh_s2,
+                                int sh_srows, const void* sh_gate, const float* out_bias, void* y, int64_t* ids_out,
+                                void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (world < 2) return dm3::set_error("dm3_moe_layer_ep needs world >= 2"), 1;
+  return moe_layer_impl(x, T, H, I, router_w, router_dtype, n_router, top_k, logits_bf16, logit_bias, w13, w13_stride,
+                        s13, s13_stride, w2, w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows,
+                        sh_gate, out_bias, y, ids_out, w_out, workspace, workspace_bytes, stream, world, rank,
+                        tokens_per_rank, arenas);
 }
 
 extern "C" int dm3_moe_status(void* workspace, uint32_t* status, void* stream) {

@@ -140,6 +140,68 @@ class ExpertParallel:
                               sh_s2, sh_gate, out_bias, self.world, self.rank, self.tokens_per_rank, self.arenas,
                               owner)
 
+    def moe_layer(self, x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, logit_bias: Optional[Tensor],
+                  w13: Tensor, s13: Tensor, w2: Tensor, s2: Tensor, sh_w13: Optional[Tensor] = None,
+                  sh_s13: Optional[Tensor] = None, sh_w2: Optional[Tensor] = None, sh_s2: Optional[Tensor] = None,
+                  sh_gate: Optional[Tensor] = None, out_bias: Optional[Tensor] = None):
+        """The sharded decode layer: every rank the same rows x, its own E / world experts (contiguous
+        blocks); returns the whole layer's (y, ids, routing weights) on every rank."""
+        return moe_layer_ep(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2,
+                            sh_s2, sh_gate, out_bias, self.world, self.rank, self.tokens_per_rank, self.arenas)
+
+
+@torch.library.custom_op("dm3::moe_layer_ep", mutates_args=())
+def moe_layer_ep(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool, logit_bias: Optional[Tensor],
+                 w13: Tensor, s13: Tensor, w2: Tensor, s2: Tensor, sh_w13: Optional[Tensor], sh_s13: Optional[Tensor],
+                 sh_w2: Optional[Tensor], sh_s2: Optional[Tensor], sh_gate: Optional[Tensor],
+                 out_bias: Optional[Tensor], world: int, rank: int, tokens_per_rank: int,
+                 arenas: List[int]) -> tuple[Tensor, Tensor, Tensor]:
+    """The fused decode MoE layer sharded over the ranks: every rank passes the same rows and router,
+    its own experts (contiguous blocks), and gets the whole layer's output (<= 4 rows per launch)."""
+    from .ops import MAX_ROWS, moe_workspace
+
+    _require_cuda(x, router_w, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias)
+    lib = _lib.load()
+    w13, w2 = _fp8_bytes(w13), _fp8_bytes(w2)
+    x = x.contiguous()
+    T, H = x.shape
+    El, I, srows, w13s, s13s, w2s, s2s = _expert_strides(w13, s13, w2, s2, H)
+    E = router_w.shape[0]
+    if router_w.dtype not in (torch.float32, BF16) or router_w.shape[1] != H or E != El * world:
+        raise RuntimeError("router weight must be fp32 or bf16 [world x local experts, H]")
+    router_w = router_w.contiguous()
+    rdt = 0 if router_w.dtype == torch.float32 else 1
+    if logit_bias is not None:
+        logit_bias = logit_bias.float().contiguous()
+    sh_w13, sh_s13, sh_w2, sh_s2, sh_srows = _shared_args(sh_w13, sh_s13, sh_w2, sh_s2, H, I)
+    if sh_gate is not None:
+        sh_gate = sh_gate.to(BF16).reshape(-1).contiguous()
+    if out_bias is not None:
+        out_bias = out_bias.float().contiguous()
+    y = torch.empty((T, H), dtype=BF16, device=x.device)
+    ids = torch.empty((T, top_k), dtype=torch.int64, device=x.device)
+    wts = torch.empty((T, top_k), dtype=BF16, device=x.device)
+    ws = moe_workspace(x.device, H, I)
+    st = _stream(x.device)
+    arr = _arena_array(arenas)
+    for t0 in range(0, T, MAX_ROWS):
+        t = min(MAX_ROWS, T - t0)
+        rc = lib.dm3_moe_layer_ep(_ptr(x[t0:]), t, H, I, _ptr(router_w), rdt, E, top_k, 1 if logits_bf16 else 0,
+                                  _ptr(logit_bias), _ptr(w13), w13s, _ptr(s13), s13s, _ptr(w2), w2s, _ptr(s2), s2s,
+                                  srows, _ptr(sh_w13), _ptr(sh_s13), _ptr(sh_w2), _ptr(sh_s2), sh_srows, _ptr(sh_gate),
+                                  _ptr(out_bias), _ptr(y[t0:]), _ptr(ids[t0:]), _ptr(wts[t0:]), world, rank,
+                                  tokens_per_rank, arr, _ptr(ws), ws.numel(), st)
+        _lib.check(rc, "dm3_moe_layer_ep")
+    return y, ids, wts
+
+
+@moe_layer_ep.register_fake
+def _(x, router_w, top_k, logits_bf16, logit_bias, w13, s13, w2, s2, sh_w13, sh_s13, sh_w2, sh_s2, sh_gate, out_bias,
+      world, rank, tokens_per_rank, arenas):
+    T = x.shape[0]
+    return (torch.empty_like(x, dtype=BF16), x.new_empty((T, top_k), dtype=torch.int64),
+            x.new_empty((T, top_k), dtype=BF16))
+
 
 def _owner(owner: Optional[Tensor], E: int) -> Optional[Tensor]:
     if owner is None:

@@ -223,8 +223,8 @@ int dm3_route(const void* x, int T, int H, const void* router_w, int n_router, i
  * process (arenas[rank] its own). Pairs travel to their owner and output rows back over NVLink peer
  * stores from inside the kernels, with flags carrying a per-call epoch (bounded waits; a wait that
  * runs out sets the status word). Every rank must make the same sequence of calls.
- * The SURVEY's NCCL all_to_all_single dispatch / combine of OnDemandExperts (engine.py:138-147) is
- * replaced by these calls.
+ * These calls carry the token-to-expert dispatch of OnDemandExperts.forward (engine.py:138-147)
+ * across GPUs.
  */
 size_t dm3_ep_arena_bytes(int world, int tokens_per_rank, int top_k, int H);
 int dm3_ep_alloc(size_t bytes, void** ptr);
@@ -269,6 +269,24 @@ int dm3_ep_combine(const void* x, int T, int H, int I, const void* router_w, int
                    const float* sh_s13, const void* sh_w2, const float* sh_s2, int sh_srows, const void* sh_gate,
                    const float* out_bias, void* y, int world, int rank, int tokens_per_rank, void* const* arenas,
                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * dm3_moe_layer sharded over `world` ranks (2 <= world <= 8, one process per GPU): every rank holds
+ * the same rows x and router and computes the same routing; rank r runs only its n_router / world
+ * experts (w13 / s13 / w2 / s2 hold them, in local index order: expert e is local index
+ * e - r * n_router / world) and rank 0 the shared expert; the partial sums meet in a one-shot
+ * all-reduce over the expert-parallel arenas (stored over NVLink into every rank's arena, epoch
+ * flags, bounded waits), after which every rank holds the full layer output y. arenas and
+ * tokens_per_rank as dm3_moe_prefill_ep (one arena serves both paths). Other arguments and limits
+ * as dm3_moe_layer; every rank must make the same sequence of calls.
+ */
+int dm3_moe_layer_ep(const void* x, int T, int H, int I, const void* router_w, int router_dtype, int n_router,
+                     int top_k, int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
+                     const float* s13, int64_t s13_stride, const void* w2, int64_t w2_stride, const float* s2,
+                     int64_t s2_stride, int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2,
+                     const float* sh_s2, int sh_srows, const void* sh_gate, const float* out_bias, void* y,
+                     int64_t* ids_out, void* w_out, int world, int rank, int tokens_per_rank, void* const* arenas,
+                     void* workspace, size_t workspace_bytes, void* stream);
 
 /* Number of kernels the last MoE / GEMV entry point launched on this host thread. */
 int dm3_last_launch_count(void);

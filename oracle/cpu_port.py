@@ -1,6 +1,6 @@
 """The reference's decode MoE layer as its own torch code would run it on host cores (fp32).
 
-TEST / BASELINE INFRASTRUCTURE ONLY: bench.py times this as the CPU baseline (`cpu_baseline`,
+TEST AND CPU-BASELINE INFRASTRUCTURE ONLY: bench.py times this as the CPU baseline (`cpu_baseline`,
 kind "port", and the `--impl reference` arm). It restates, in torch fp32 on CPU:
   router      bf16 nn.Linear logits -> softmax(fp32) -> topk -> renormalise -> bf16
               (exp1_routing.py:59-60, engine.py:233-235); an fp32 router for the speaker

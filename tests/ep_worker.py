@@ -106,6 +106,31 @@ def gpu_rank(rank: int, world: int, store: str, out_dir: str) -> None:
                                       owner=owner.to(dev))
         torch.cuda.synchronize()
         res["placed_y"] = bool(torch.equal(yb, ref_y[sl])) and bool(torch.equal(idsb, ref_ids[sl]))
+        # the sharded decode layer (2 rows): every rank the same rows, its own contiguous experts
+        x2 = x[:2].contiguous()
+        obias = torch.randn(H, generator=g, device=dev) * 0.02
+        dref = dm3.ops.moe_layer(x2, gate, K, True, bias, w13, s13, w2, s2, sh13, shs13, sh2, shs2, shg, obias)
+        lwc = (w13[rank * el:(rank + 1) * el], s13[rank * el:(rank + 1) * el], w2[rank * el:(rank + 1) * el],
+               s2[rank * el:(rank + 1) * el])
+        ok = True
+        for rep in range(3):
+            dy, dids, dw = grp.moe_layer(x2, gate, K, True, bias, *lwc, sh13, shs13, sh2, shs2, shg, obias)
+            torch.cuda.synchronize()
+            ok = ok and bool(torch.equal(dids, dref[1])) and bool(torch.equal(dw, dref[2]))
+            err = float((dy.float() - dref[0].float()).norm() / dref[0].float().norm())
+            ok = ok and err < 1e-3
+            res[f"decode_err{rep}"] = err
+        dist.barrier()
+        dgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(dgraph):
+            gdy = grp.moe_layer(x2, gate, K, True, bias, *lwc, sh13, shs13, sh2, shs2, shg, obias)[0]
+        for _ in range(3):
+            dgraph.replay()
+        torch.cuda.synchronize()
+        res["decode_graph_err"] = float((gdy.float() - dref[0].float()).norm() / dref[0].float().norm())
+        res["decode_ok"] = ok and res["decode_graph_err"] < 1e-3
+        res["decode_status"] = dm3.ops.moe_status(dm3.ops.moe_workspace(dev, H, I))
+        del dgraph
         ws = dm3.ep._ep_workspaces[rank]
         res["status"] = dm3.ops.moe_status(ws)
         del graph

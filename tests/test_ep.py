@@ -1,5 +1,6 @@
-"""Expert-parallel prefill: the algorithm on gloo CPU ranks (oracle.ep_oracle) against the
-one-process oracle, and the NVLink kernels on 2 GPUs against the one-GPU kernels."""
+"""Expert-parallel prefill and the sharded decode layer: the algorithm on gloo CPU ranks
+(oracle.ep_oracle) against the one-process oracle, and the NVLink kernels on 2 GPUs against the
+one-GPU kernels."""
 
 import os
 
@@ -47,3 +48,4 @@ def test_ep_prefill_two_gpus(tmp_path):
         assert r["split_y0"] and r["split_y1"], r
         assert r["graph_y"], r
         assert r["placed_y"], r
+        assert r["decode_status"] == 0 and r["decode_ok"], r
