@@ -41,6 +41,15 @@ bool pdl_enabled() {
   return v == 1;
 }
 
+bool cluster_path_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("DM3_CLUSTER");
+    v = (e && std::strcmp(e, "1") == 0) ? 1 : 0;
+  }
+  return v == 1;
+}
+
 namespace {
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

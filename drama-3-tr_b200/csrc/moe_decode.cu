@@ -68,6 +68,8 @@ struct Params {
   int T, H, I, top_k;
   const __nv_bfloat16* x;
   int mode;  // 0 = routing given (ids/weights), 1 = router in-kernel
+  int fused;  // 1: the cluster kernel (layer_kernel) selects experts and combines; the route kernel only
+              // computes logits and splits x
   const int64_t* ids;
   const __nv_bfloat16* rw;
   const void* router_w;
@@ -109,9 +111,11 @@ struct Params {
 // serves every T of a given (H, I). Nothing in it carries state from one call to the next except
 // the sticky status word (the route kernel's CTA counter is back at zero after every call).
 struct WsLayout {
-  size_t ctrl, slot_expert, coef, gate, logits, himg, himg_stride, hinv, ximg, xinv, partial, total;
+  size_t ctrl, slot_expert, coef, gate, logits, himg, himg_stride, hinv, ximg, xinv, partial, facc, total;
 };
-enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
+// CTRL_FCOUNT: CTAs of the cluster kernel that have added their partial sums (back at zero after
+// every call)
+enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_FCOUNT = 6, CTRL_WORDS = 16 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -145,6 +149,9 @@ __host__ __device__ inline WsLayout ws_layout(int H, int I) {
   o = align_up(o, 128);
   L.partial = o;  // [H / 128][kMaxSlots][kMaxT][128] fp32: one output block's slots are adjacent
   o += static_cast<size_t>(H / kBlockRows) * kMaxSlots * kMaxT * kBlockRows * 4;
+  o = align_up(o, 256);
+  L.facc = o;  // [2][kMaxT][H] int64: the cluster kernel's fixed-point sums (routed, shared); zero between calls
+  o += static_cast<size_t>(2) * kMaxT * H * 8;
   L.total = align_up(o, 256);
   return L;
 }
@@ -349,7 +356,7 @@ __device__ __forceinline__ void warp_top8_32(uint32_t (&k)[8]) {
 // ties to the lower index: keys pack (logit order, ~index) so one comparison decides both. When
 // every logit is a bf16 value (bf16 logits without a bias) the order fits 16 bits and a key is
 // 32 bits; otherwise 64.
-__device__ void route_row(const Params& p, RouteTail& rt, int t, int lane) {
+__device__ void route_row(const Params& p, RouteTail& rt, int t, int lane, bool emit = true) {
   const int E = p.n_router, K = p.top_k;
   float lv[8];
   float mloc = -FLT_MAX;
@@ -418,8 +425,8 @@ __device__ void route_row(const Params& p, RouteTail& rt, int t, int lane) {
     const __nv_bfloat16 wb = __float2bfloat16_rn(my_p / psum);
     rt.sel_e[t * K + lane] = my_e;
     rt.sel_w[t * K + lane] = __bfloat162float(wb);
-    if (p.ids_out) p.ids_out[t * K + lane] = my_e;
-    if (p.w_out) p.w_out[t * K + lane] = wb;
+    if (emit && p.ids_out) p.ids_out[t * K + lane] = my_e;
+    if (emit && p.w_out) p.w_out[t * K + lane] = wb;
   }
   if (lane == 0) rt.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-rt.logits[t][E]))) : 1.f;
 }
@@ -630,6 +637,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
       logits[t * (kMaxRouter + 1) + row0 + r] = v;
     }
   }
+  if (p.fused) return;  // the cluster kernel reads the logits once this kernel has completed
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -1202,6 +1210,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
   p.y[static_cast<size_t>(t) * p.H + n] = __float2bfloat16_rn(acc);
 }
 
+#include "moe_cluster.cuh"
+
 }  // namespace moe
 }  // namespace dm3
 
@@ -1262,6 +1272,10 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
     }
     ok = ok && cudaFuncSetAttribute(moe::combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     cudaSharedmemCarveoutMaxShared) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(moe::layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    227 * 1024) == cudaSuccess;
+    ok = ok && cudaFuncSetAttribute(moe::layer_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared) == cudaSuccess;
     if (!ok) {
       set_error("cudaFuncSetAttribute(moe) failed");
       return 2;
@@ -1288,6 +1302,38 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
   }
   const int sms = sm_count(dev);
   int launches = 0;
+  if (p.fused) {
+    // route (logits + x split), then the cluster kernel: one cluster of kCl CTAs per (possible slot,
+    // quarter of I)
+    const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
+    const bool w32 = p.router_bf16 == 0;
+    if (int rc = launch_one(w32 ? moe::route_kernel<true> : moe::route_kernel<false>,
+                            (rows + moe::kRouteWarps - 1) / moe::kRouteWarps, moe::kRouteThreads,
+                            moe::route_smem_bytes(p.H, w32), stream, "moe route", p))
+      return rc;
+    const int clusters = (p.T * p.top_k + (p.sh_slot ? 1 : 0)) * (p.I / 128);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(clusters * moe::kCl);
+    cfg.blockDim = dim3(moe::kThreads);
+    cfg.dynamicSmemBytes = moe::fsmem_layout(p.H, p.I).total;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = moe::kCl;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, moe::layer_kernel, p, m13, m2, msh13, msh2);
+    if (err != cudaSuccess) {
+      set_error(std::string("moe cluster launch: ") + cudaGetErrorString(err));
+      return 2;
+    }
+    note_launches(2);
+    return 0;
+  }
   if (p.mode == 1) {
     const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
     const bool w32 = p.router_bf16 == 0;
@@ -1444,6 +1490,8 @@ static int moe_layer_impl(const void* x, int T, int H, int I, const void* router
     p.n_experts = p.ep_el;  // w13 / w2 hold this rank's experts
     for (int r = 0; r < 8; ++r) p.ep_arena[r] = r < world ? static_cast<uint8_t*>(arenas[r]) : nullptr;
   }
+  // one kernel of thread-block clusters for the expert phase where the shape allows it
+  p.fused = world <= 1 && dm3::moe::cluster_shape_ok(H, I) && dm3::cluster_path_enabled() ? 1 : 0;
   return dm3::launch_moe(p, static_cast<cudaStream_t>(stream));
 }
 
