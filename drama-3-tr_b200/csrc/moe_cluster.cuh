@@ -163,6 +163,14 @@ __device__ int table_smem(const Params& p, RouteTail& rt, int lane, Table& tab) 
   return base + total;
 }
 
+// Makes the loaded values of v live here, so that their loads are complete before a long wait
+// rather than being sunk past it by the compiler.
+template <int N>
+__device__ __forceinline__ void hold(const float (&v)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" ::"f"(v[i]));
+}
+
 // The four epilogue warps wait for one mbarrier phase (lane 0 of each, bounded) and continue only
 // if all four waits succeeded: a uniform decision, so no warp is left alone at a named barrier.
 __device__ __forceinline__ bool epi_wait_all(FAux& aux, uint64_t* bar, uint32_t parity, bool cluster_scope, int e,
@@ -213,7 +221,7 @@ __device__ void cl_epilogue_up(const Params& p, FAux& aux, uint8_t* hb, uint32_t
         hv[t] = bf16_round(gt * __frcp_rn(1.f + __expf(-gt)) * ut);
       }
     }
-    const uint32_t am = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(hv[t])));
+    const uint32_t am = t < p.T ? __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(hv[t]))) : 0u;
     if (lane == 0) aux.hmax[e][t] = am;
   }
   named_bar(kBarGate, 2 * 32);
@@ -248,22 +256,37 @@ __device__ void cl_epilogue_up(const Params& p, FAux& aux, uint8_t* hb, uint32_t
   }
 }
 
-// Down: thread r holds output row `row` for the quarter's 128 k; its two accumulators (16 TMEM
-// columns each) cover the 64 columns of h from CTA 0 and from CTA 1 of the cluster, each with its
-// own 2^-e; sc is the weight's 128-block scale. The contribution (times the routing weight; the
-// shared expert's stays raw) is added to the fixed-point sums of its row.
+// Down, for kB consecutive 128-row blocks (nb of them valid) of this CTA: thread r holds output row
+// rows0 + 128 b + r of block b for the quarter's 128 k. A block's two accumulators (16 TMEM columns
+// each) cover the 64 columns of h from CTA 0 and from CTA 1 of the cluster, each with its own 2^-e;
+// sc[b] is the weight's 128-block scale. Every accumulator of the batch is read before the first
+// wait. The contributions (times the routing weight; the shared expert's stay raw) are added to the
+// fixed-point sums of their rows.
+template <int kB>
 __device__ __forceinline__ void cl_epilogue_down(const Params& p, const WsLayout& L, FAux& aux, uint32_t taddr,
-                                                 int slot, bool shared_slot, int row, float sc) {
-  float v0[8], v1[8];
-  tc::tmem_ld8(taddr, v0);
-  tc::tmem_ld8(taddr + 16, v1);
+                                                 int slot, bool shared_slot, int row0, const float* sc, int nb) {
+  float v[kB][2][8];
+#pragma unroll
+  for (int b = 0; b < kB; ++b)
+    if (b < nb) {
+      tc::tmem_ld8(taddr + 32u * b, v[b][0]);
+      tc::tmem_ld8(taddr + 32u * b + 16u, v[b][1]);
+    }
   tc::tmem_wait_ld();
   unsigned long long* fa = reinterpret_cast<unsigned long long*>(p.ws + L.facc) +
-                           static_cast<size_t>(shared_slot ? kMaxT : 0) * p.H + row;
-  for (int t = 0; t < p.T; ++t) {
-    float y = sc * fmaf(aux.hexp[0][t], v0[t] + v0[4 + t], aux.hexp[1][t] * (v1[t] + v1[4 + t]));
-    if (!shared_slot) y *= aux.tab.coef[slot * kMaxT + t];
-    atomicAdd(fa + static_cast<size_t>(t) * p.H, static_cast<unsigned long long>(__float2ll_rn(y * kFixScale)));
+                           static_cast<size_t>(shared_slot ? kMaxT : 0) * p.H + row0;
+#pragma unroll
+  for (int t = 0; t < kMaxT; ++t) {
+    if (t >= p.T) break;
+    const float h0 = aux.hexp[0][t], h1 = aux.hexp[1][t];
+    const float cf = shared_slot ? 1.f : aux.tab.coef[slot * kMaxT + t];
+#pragma unroll
+    for (int b = 0; b < kB; ++b)
+      if (b < nb) {
+        const float y = sc[b] * fmaf(h0, v[b][0][t] + v[b][0][4 + t], h1 * (v[b][1][t] + v[b][1][4 + t])) * cf;
+        atomicAdd(fa + static_cast<size_t>(t) * p.H + kBlockRows * b,
+                  static_cast<unsigned long long>(__float2ll_rn(y * kFixScale)));
+      }
   }
 }
 
@@ -527,20 +550,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = row_base + kBlockRows * j + r;
         sc2[j] = j < ntiles ? __ldg(ex.s2 + static_cast<size_t>(row / ex.srows) * nq + quarter) : 0.f;
       }
+      hold(sc13);
+      hold(sc2);
       bool ok = epi_wait_all(aux, &aux.acc_full, 0, false, e, lane);
       if (ok) {
         tc::fence_after_sync();
         cl_epilogue_up(p, aux, smem + S.hb, tmem + tlane, shared_slot, q, e, lane, sc13);
         ok = epi_wait_all(aux, &aux.hx_full, 0, true, e, lane);
       }
+      // four blocks at a time: the MMAs are committed in order, so block j + 3's barrier covers the
+      // batch, and the first batch is read while the MMAs of the second are issued
 #pragma unroll
-      for (int j = 0; j < kFMaxTiles; ++j) {
+      for (int j = 0; j < kFMaxTiles; j += 4) {
         if (!ok || j >= ntiles) break;
-        ok = epi_wait_all(aux, &aux.dacc_full[j], 0, false, e, lane);
+        ok = epi_wait_all(aux, &aux.dacc_full[min(j + 3, ntiles - 1)], 0, false, e, lane);
         if (!ok) break;
         tc::fence_after_sync();
-        cl_epilogue_down(p, L, aux, tmem + tlane + 256u + 32u * j, slot, shared_slot, row_base + kBlockRows * j + r,
-                         sc2[j]);
+        cl_epilogue_down<4>(p, L, aux, tmem + tlane + 256u + 32u * j, slot, shared_slot, row_base + kBlockRows * j + r,
+                            &sc2[j], min(4, ntiles - j));
       }
       if (ok) {
         // count this CTA's sums; the last CTA of the call converts them (after the barrier below)

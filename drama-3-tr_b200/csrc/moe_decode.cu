@@ -30,6 +30,7 @@
 // only after its own griddepcontrol.wait, so once a kernel is running, everything two launches
 // back has completed. The down kernel relies on that to select experts before its wait.
 #include <cfloat>
+#include <cstddef>
 #include <cmath>
 #include <utility>
 
@@ -312,15 +313,17 @@ __device__ int table_from_ws(const Params& p, const WsLayout& L, int lane, Table
 // Shared-memory tail of the route kernel: the logits of every row (the last column is the shared
 // expert's gate), the selections and the table scratch of the last CTA.
 struct RouteTail {
-  float2 part[kRouteWarps][kMaxT][kRouteSplit];  // (hi, lo) of each warp's quarter of a row
+  // the fields the route kernel itself uses come first: with a cluster kernel after it, the route
+  // kernel's shared memory ends at `logits`
+  uint64_t bar;
+  int last;
   uint32_t xmax[kMaxT];
+  float2 part[kRouteWarps][kMaxT][kRouteSplit];  // (hi, lo) of each warp's quarter of a row
   float logits[kMaxT][kMaxRouter + 1];
   int sel_e[kMaxT * kMaxTopK];
   float sel_w[kMaxT * kMaxTopK];
   float shared_coef[kMaxT];
   uint32_t bitmap[kMaxRouter / 32];
-  uint64_t bar;
-  int last;
 };
 
 __device__ __forceinline__ void cswap_desc32(uint32_t& a, uint32_t& b) {
@@ -480,11 +483,14 @@ __device__ __forceinline__ void two_sum_acc(float& hi, float& lo, float a) {
 
 // Shared memory of the route kernel: the CTA's router rows (staged by bulk copies before the
 // wait), the activation rows, then RouteTail.
-__host__ __device__ inline size_t route_tail_offset(int H, bool w32) {
-  return align_up(static_cast<size_t>(kRouteWarps) * H * (w32 ? 4 : 2) + static_cast<size_t>(kMaxT) * H * 2, 16);
+// rw router rows per CTA, T activation rows.
+__host__ __device__ inline size_t route_tail_offset(int H, bool w32, int rw, int T) {
+  return align_up(static_cast<size_t>(rw) * H * (w32 ? 4 : 2) + static_cast<size_t>(T) * H * 2, 16);
 }
-__host__ __device__ inline size_t route_smem_bytes(int H, bool w32) {
-  return route_tail_offset(H, w32) + align_up(sizeof(RouteTail), 16);
+// The route kernel's shared memory; `fused` (a cluster kernel follows) needs no selection scratch,
+// which keeps a route CTA small enough to sit on an SM beside a cluster CTA of the previous layer.
+__host__ __device__ inline size_t route_smem_bytes(int H, bool w32, int rw, int T, bool fused) {
+  return route_tail_offset(H, w32, rw, T) + align_up(fused ? offsetof(RouteTail, logits) : sizeof(RouteTail), 16);
 }
 
 // Router logits, then the route table. Four warps per router row (plus the shared expert's gate
@@ -497,8 +503,9 @@ __host__ __device__ inline size_t route_smem_bytes(int H, bool w32) {
 // Each CTA also splits its share of x into the up kernel's activation tile (the exact e4m3 hi / lo
 // of x * 2^e per row). The last CTA to finish (one gpu-scope fence per CTA, with no copies in
 // flight) selects the experts of every row (one warp per row) and writes the table.
-template <bool W32>
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_constant__ Params p) {
+template <bool W32, int RW>
+__global__ void __launch_bounds__(RW * kRouteSplit * 32) route_kernel(const __grid_constant__ Params p) {
+  constexpr int kThr = RW * kRouteSplit * 32;
   extern __shared__ __align__(16) uint8_t rsm[];
   const WsLayout L = ws_layout(p.H, p.I);
   const int H = p.H;
@@ -506,19 +513,19 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
   const int rw = warp / kRouteSplit, quarter = warp % kRouteSplit;  // row within the CTA, quarter of H
   const bool sh_gate_row = p.sh_w13 != nullptr && p.sh_gate != nullptr;
   const int rows = p.n_router + (sh_gate_row ? 1 : 0);
-  const int row0 = blockIdx.x * kRouteWarps;
+  const int row0 = blockIdx.x * RW;
   const int row = row0 + rw;
   const int wsz = W32 ? 4 : 2;
-  uint8_t* wrows = rsm;  // [kRouteWarps][H] weights
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm + static_cast<size_t>(kRouteWarps) * H * wsz);
-  RouteTail& rt = *reinterpret_cast<RouteTail*>(rsm + route_tail_offset(H, W32));
+  uint8_t* wrows = rsm;  // [RW][H] weights
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm + static_cast<size_t>(RW) * H * wsz);
+  RouteTail& rt = *reinterpret_cast<RouteTail*>(rsm + route_tail_offset(H, W32, RW, p.T));
   if (threadIdx.x == 0) {
     mbar_init(&rt.bar, 1);
     fence_mbar_init();
     uint32_t bytes = 0;
-    for (int r = row0; r < min(rows, row0 + kRouteWarps); ++r) bytes += r < p.n_router ? H * wsz : H * 2;
+    for (int r = row0; r < min(rows, row0 + RW); ++r) bytes += r < p.n_router ? H * wsz : H * 2;
     mbar_arrive_expect_tx(&rt.bar, bytes);
-    for (int r = row0; r < min(rows, row0 + kRouteWarps); ++r) {
+    for (int r = row0; r < min(rows, row0 + RW); ++r) {
       if (r < p.n_router)
         bulk_g2s(wrows + static_cast<size_t>(r - row0) * H * wsz,
                  static_cast<const uint8_t*>(p.router_w) + static_cast<size_t>(r) * H * wsz, H * wsz, &rt.bar);
@@ -531,25 +538,27 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
   griddep_wait();
   griddep_launch();
   {
-    constexpr int kPer = kMaxT * kMaxH / 8 / kRouteThreads;
+    constexpr int kPer = kMaxT * kMaxH / 8 / kThr;
     const int n16 = p.T * H / 8;
     const uint4* xsrc = reinterpret_cast<const uint4*>(p.x);
     uint4 v[kPer];
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int c = threadIdx.x + q * kRouteThreads;
+      const int c = threadIdx.x + q * kThr;
       v[q] = c < n16 ? xsrc[c] : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int c = threadIdx.x + q * kRouteThreads;
+      const int c = threadIdx.x + q * kThr;
       if (c < n16) {
         reinterpret_cast<uint4*>(xs)[c] = v[q];
         const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[q]);
         float m = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(__bfloat162float(e[i])));
-        atomicMax(&rt.xmax[c / (H / 8)], __float_as_uint(m));
+        // a warp's chunks lie in one row (H / 8 is a multiple of 32): one shared atomic per warp
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+        if (lane == 0) atomicMax(&rt.xmax[c / (H / 8)], wm);
       }
     }
   }
@@ -560,7 +569,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
     uint8_t* img = p.ws + L.ximg;
     const int chunks = H / 16;
     for (int c = blockIdx.x + gridDim.x * static_cast<int>(threadIdx.x); c < p.T * chunks;
-         c += gridDim.x * kRouteThreads) {
+         c += gridDim.x * kThr) {
       const int t = c / chunks, k = (c % chunks) * 16;
       const uint4 v2[2] = {*reinterpret_cast<const uint4*>(xs + t * H + k), *reinterpret_cast<const uint4*>(xs + t * H + k + 8)};
       uint4 hi, lo;
@@ -618,7 +627,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
     }
   }
   __syncthreads();
-  if (threadIdx.x < kRouteWarps * kMaxT) {
+  if (threadIdx.x < RW * kMaxT) {
     const int r = threadIdx.x / kMaxT, t = threadIdx.x % kMaxT;
     if (row0 + r < rows && t < p.T) {
       float h = rt.part[r][t][0].x, l = rt.part[r][t][0].y;
@@ -649,16 +658,16 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const __grid_const
   if (!rt.last) return;
   // last CTA: every logit is visible
   {
-    constexpr int kPer = (kMaxT * (kMaxRouter + 1) + kRouteThreads - 1) / kRouteThreads;
+    constexpr int kPer = (kMaxT * (kMaxRouter + 1) + kThr - 1) / kThr;
     float v[kPer];
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int i = threadIdx.x + q * kRouteThreads;
+      const int i = threadIdx.x + q * kThr;
       v[q] = i < p.T * (kMaxRouter + 1) && i % (kMaxRouter + 1) < rows ? __ldcg(logits + i) : 0.f;
     }
 #pragma unroll
     for (int q = 0; q < kPer; ++q) {
-      const int i = threadIdx.x + q * kRouteThreads;
+      const int i = threadIdx.x + q * kThr;
       if (i < kMaxT * (kMaxRouter + 1)) (&rt.logits[0][0])[i] = v[q];
     }
   }
@@ -1264,9 +1273,11 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
                                     cudaSharedmemCarveoutMaxShared) == cudaSuccess;
     ok = ok && cudaFuncSetAttribute(moe::expert_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     cudaSharedmemCarveoutMaxShared) == cudaSuccess;
-    for (auto k : {moe::route_kernel<false>, moe::route_kernel<true>}) {
+    for (auto k : {moe::route_kernel<false, 4>, moe::route_kernel<true, 4>, moe::route_kernel<false, 2>,
+                   moe::route_kernel<true, 2>}) {
       ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(moe::route_smem_bytes(kMaxH, true))) == cudaSuccess;
+                                      static_cast<int>(moe::route_smem_bytes(kMaxH, true, 4, kMaxT, false))) ==
+                     cudaSuccess;
       ok = ok && cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
                                       cudaSharedmemCarveoutMaxShared) == cudaSuccess;
     }
@@ -1307,9 +1318,10 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
     // quarter of I)
     const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
     const bool w32 = p.router_bf16 == 0;
-    if (int rc = launch_one(w32 ? moe::route_kernel<true> : moe::route_kernel<false>,
-                            (rows + moe::kRouteWarps - 1) / moe::kRouteWarps, moe::kRouteThreads,
-                            moe::route_smem_bytes(p.H, w32), stream, "moe route", p))
+    // two router rows per CTA: one small route CTA per SM, beside the previous layer's cluster CTA
+    if (int rc = launch_one(w32 ? moe::route_kernel<true, 2> : moe::route_kernel<false, 2>, (rows + 1) / 2,
+                            2 * moe::kRouteSplit * 32, moe::route_smem_bytes(p.H, w32, 2, p.T, true), stream,
+                            "moe route", p))
       return rc;
     const int clusters = (p.T * p.top_k + (p.sh_slot ? 1 : 0)) * (p.I / 128);
     cudaLaunchConfig_t cfg{};
@@ -1337,9 +1349,9 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
   if (p.mode == 1) {
     const int rows = p.n_router + (p.sh_w13 && p.sh_gate ? 1 : 0);
     const bool w32 = p.router_bf16 == 0;
-    if (int rc = launch_one(w32 ? moe::route_kernel<true> : moe::route_kernel<false>,
+    if (int rc = launch_one(w32 ? moe::route_kernel<true, 4> : moe::route_kernel<false, 4>,
                             (rows + moe::kRouteWarps - 1) / moe::kRouteWarps, moe::kRouteThreads,
-                            moe::route_smem_bytes(p.H, w32), stream, "moe route", p))
+                            moe::route_smem_bytes(p.H, w32, moe::kRouteWarps, p.T, false), stream, "moe route", p))
       return rc;
     ++launches;
   }
