@@ -45,7 +45,7 @@ bool cluster_path_enabled() {
   static int v = -1;
   if (v < 0) {
     const char* e = std::getenv("DM3_CLUSTER");
-    v = (e && std::strcmp(e, "1") == 0) ? 1 : 0;
+    v = (e && std::strcmp(e, "0") == 0) ? 0 : 1;
   }
   return v == 1;
 }

@@ -22,8 +22,8 @@ void set_error(const std::string& msg);
 int sm_count(int device);
 void note_launches(int n);
 bool pdl_enabled();
-// The decode layer's expert phase as one kernel of thread-block clusters (DM3_CLUSTER=1; the
-// four-kernel chain otherwise).
+// The decode layer's expert phase as one kernel of thread-block clusters (the default; DM3_CLUSTER=0
+// selects the four-kernel chain).
 bool cluster_path_enabled();
 // A 3-D uint8 tensor map over [d2][d1][d0] bytes (row stride stride1, plane stride stride2) whose
 // box is 128 bytes x box_rows rows x 1 plane, loaded with the 128-byte swizzle; encodings are cached

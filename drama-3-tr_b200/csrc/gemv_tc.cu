@@ -111,6 +111,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
 
   if (warp == 0) {
     if (lane == 0) {
+      // the next kernel may start as soon as every CTA of this one runs: in a chain of GEMVs its weight
+      // copies then overlap this one (each kernel still waits for its predecessor's completion before
+      // touching x or y, so the data order is unchanged)
+      griddep_launch();
       mbar_arrive_expect_tx(&aux.full, static_cast<uint32_t>(nsl * kSlabBytes));
       for (int j = 0; j < nsl; ++j)
         tc::tma_load_3d(a_tiles + j * kSlabBytes, &map_q, k0 + j * 128, tile * kTileRows, 0, &aux.full);
@@ -120,7 +124,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
     // x chunk -> activation tile (rows t: hi, 4 + t: lo; other rows only feed unread columns)
     const int sidx = tid - 64;
     griddep_wait();
-    griddep_launch();
     const int chunks = kchunk / 16, n = p.M * chunks;
     constexpr int kMaxTasks = kMaxT * (kMaxSlabs * 128 / 16) / kSplitThreads;
     uint4 v[kMaxTasks][2];
@@ -154,7 +157,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
     tc::fence_proxy_async_smem();
   } else if (warp >= 4) {
     griddep_wait();  // y may be read by the preceding kernel's consumers until it completes
-    griddep_launch();
   }
   __syncthreads();  // activation tile written (and fenced for the tensor core), xinv set
 

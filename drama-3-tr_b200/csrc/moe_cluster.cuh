@@ -17,8 +17,11 @@
 //         behind the up slabs and are already in shared memory when h arrives;
 //   sum   every output element's contribution is added as a 64-bit fixed-point integer (2^-36
 //         units) into the workspace with a reduction in L2: integer addition is exact and
-//         associative, so the sum does not depend on arrival order (deterministic). The CTA that
-//         counts last converts the sums to y with the reference's rounding points and clears them.
+//         associative, so the sum does not depend on arrival order (deterministic). For each half
+//         of the output rows, the CTA that counts last converts its sums to y with the reference's
+//         rounding points and clears them.
+//
+// Warps 2-3 split x into the up MMAs' B operand themselves while warps 4-7 select the experts.
 //
 // Every CTA selects the experts itself from the route kernel's logits (one warp per row, the same
 // code as the route kernel's tail), so no single-CTA step sits between the router and the first
@@ -37,6 +40,7 @@ constexpr int kBarGate = 4;             // named barrier of the 64 gate-row thre
 constexpr int kHxRows = 8;              // B rows of h sent: hi of rows 0-3, lo of rows 0-3
 constexpr uint32_t kHxBytesPerSrc = kHxRows * kUpHalf + 16;  // h bytes + the exponent vector
 constexpr float kFixScale = 68719476736.0f;                  // 2^36 fixed-point units per 1.0
+constexpr int kTableThreads = kThreads - 64;                  // the table barrier: all warps but 2-3
 
 // Barriers and small state of the cluster kernel.
 struct FAux {
@@ -52,6 +56,7 @@ struct FAux {
   float xinv[kMaxT];
   float upv[kUpHalf][kMaxT];
   uint32_t hmax[2][kMaxT];            // |h| maxima of the two gate warps
+  uint32_t xmax[kMaxT];               // |x| maxima (float bits) of the x split
   alignas(16) float hexp[kCl][kMaxT];             // 2^-e of each source CTA's columns of h, per row
   alignas(16) uint8_t hstage[kHxRows][kUpHalf];   // this CTA's h bytes before they are sent
   Table tab;
@@ -290,47 +295,107 @@ __device__ __forceinline__ void cl_epilogue_down(const Params& p, const WsLayout
   }
 }
 
-// The sums to y, by every thread of the CTA that counted last, with the rounding points of
-// combine_kernel: y = bf16(bf16(bf16(routed) + bias) + bf16(sigmoid gate * bf16(shared))); the
-// sums are cleared for the next call. Eight pairs of elements per thread and pass, every load of a
-// pass issued first.
-__device__ void cl_finish(const Params& p, const WsLayout& L, const FAux& aux, int tid) {
-  constexpr int kB = 8;
+// The sums of output rows [half H/2, half H/2 + H/2) to y, by every thread of the CTA that counted
+// last for that half, with the rounding points of combine_kernel:
+// y = bf16(bf16(bf16(routed) + bias) + bf16(sigmoid gate * bf16(shared))); the sums are cleared for
+// the next call. A sum converts to fp32 with one rounding (int64 -> float, then an exact 2^-36).
+// Four pairs of elements per thread and pass, every load of a pass issued first.
+__device__ void cl_finish(const Params& p, const WsLayout& L, const FAux& aux, int tid, int half) {
+  constexpr int kB = 4;
   long long* fa = reinterpret_cast<long long*>(p.ws + L.facc);
   const size_t shared_off = static_cast<size_t>(kMaxT) * p.H;
-  const int n_out = p.T * p.H;
+  const int hh = p.H / 2, n_out = p.T * hh;
   const bool sh = p.sh_w13 != nullptr;
-  const double unit = 1.0 / 68719476736.0;  // 2^-36
+  const float unit = 1.0f / kFixScale;
   for (int i0 = 0; i0 < n_out; i0 += kThreads * 2 * kB) {
     longlong2 R[kB], S[kB];
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
-      const int idx = i0 + (b * kThreads + tid) * 2;
-      if (idx < n_out) {
-        R[b] = __ldcg(reinterpret_cast<const longlong2*>(fa + idx));
-        S[b] = __ldcg(reinterpret_cast<const longlong2*>(fa + shared_off + idx));
+      const int i = i0 + (b * kThreads + tid) * 2;
+      if (i < n_out) {
+        const int off = (i / hh) * p.H + half * hh + i % hh;
+        R[b] = __ldcg(reinterpret_cast<const longlong2*>(fa + off));
+        S[b] = __ldcg(reinterpret_cast<const longlong2*>(fa + shared_off + off));
       }
     }
 #pragma unroll
     for (int b = 0; b < kB; ++b) {
-      const int idx = i0 + (b * kThreads + tid) * 2;
-      if (idx >= n_out) continue;
-      const int t = idx / p.H, n = idx % p.H;
-      float out[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const float rs = static_cast<float>(static_cast<double>(u ? R[b].y : R[b].x) * unit);
-        const float ss = static_cast<float>(static_cast<double>(u ? S[b].y : S[b].x) * unit);
-        float y = bf16_round(rs);
-        if (p.out_bias) y = bf16_round(y + __ldg(p.out_bias + n + u));
-        if (sh) y += bf16_round(aux.rt.shared_coef[t] * bf16_round(ss));
-        out[u] = y;
+      const int i = i0 + (b * kThreads + tid) * 2;
+      if (i >= n_out) break;
+      const int t = i / hh, n = half * hh + i % hh, off = t * p.H + n;
+      const float g = sh ? aux.rt.shared_coef[t] : 0.f;
+      float y0 = bf16_round(__ll2float_rn(R[b].x) * unit), y1 = bf16_round(__ll2float_rn(R[b].y) * unit);
+      if (p.out_bias) {
+        y0 = bf16_round(y0 + __ldg(p.out_bias + n));
+        y1 = bf16_round(y1 + __ldg(p.out_bias + n + 1));
       }
-      *reinterpret_cast<__nv_bfloat162*>(p.y + idx) = __floats2bfloat162_rn(out[0], out[1]);
-      __stcg(reinterpret_cast<longlong2*>(fa + idx), make_longlong2(0, 0));
-      __stcg(reinterpret_cast<longlong2*>(fa + shared_off + idx), make_longlong2(0, 0));
+      if (sh) {
+        y0 += bf16_round(g * bf16_round(__ll2float_rn(S[b].x) * unit));
+        y1 += bf16_round(g * bf16_round(__ll2float_rn(S[b].y) * unit));
+      }
+      *reinterpret_cast<__nv_bfloat162*>(p.y + off) = __floats2bfloat162_rn(y0, y1);
+      __stcg(reinterpret_cast<longlong2*>(fa + off), make_longlong2(0, 0));
+      __stcg(reinterpret_cast<longlong2*>(fa + shared_off + off), make_longlong2(0, 0));
     }
   }
+}
+
+// x split into the up MMAs' B operand by the 64 threads of warps 2-3 (which are otherwise idle while
+// the experts are selected): row t holds the e4m3 hi part of x[t] * 2^e_t (e_t maps the row's
+// absolute maximum into [128, 256)), row 4 + t the lo remainder; rows of absent tokens and rows 8-15
+// only feed accumulator columns that nothing reads. The threads fence their writes for the tensor
+// core, then thread 0 arrives on xb_ready.
+__device__ void cl_split_x(const Params& p, uint8_t* bt, FAux& aux, int sidx) {
+  constexpr int kNT = 64;
+  constexpr int kMaxTasks = kMaxT * (kMaxH / 16) / kNT;
+  const int chunks = p.H / 16, n = p.T * chunks;
+  if (sidx < kMaxT) aux.xmax[sidx] = 0u;
+  named_bar(kBarSplit, kNT);
+  uint4 v[kMaxTasks][2];
+#pragma unroll
+  for (int q = 0; q < kMaxTasks; ++q) {
+    const int task = sidx + q * kNT;
+    if (task < n) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(task / chunks) * p.H + (task % chunks) * 16);
+      v[q][0] = src[0];
+      v[q][1] = src[1];
+    }
+  }
+  // this thread's maximum per row, then one warp reduction and one atomic per row
+  float m[kMaxT] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < kMaxTasks; ++q) {
+    const int task = sidx + q * kNT;
+    if (task < n) {
+      const int t = task / chunks;
+      const float a = abs_max16(v[q]);
+#pragma unroll
+      for (int u = 0; u < kMaxT; ++u)
+        if (u == t) m[u] = fmaxf(m[u], a);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kMaxT; ++t) {
+    if (t >= p.T) break;
+    const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m[t]));
+    if ((sidx & 31) == 0) atomicMax(&aux.xmax[t], wm);
+  }
+  named_bar(kBarSplit, kNT);
+  if (sidx < kMaxT) aux.xinv[sidx] = exp2i(-split_exponent(__uint_as_float(aux.xmax[sidx])));
+#pragma unroll
+  for (int q = 0; q < kMaxTasks; ++q) {
+    const int task = sidx + q * kNT;
+    if (task < n) {
+      const int t = task / chunks, c = task % chunks;
+      uint4 hi, lo;
+      split16(v[q], exp2i(split_exponent(__uint_as_float(aux.xmax[t]))), hi, lo);
+      *reinterpret_cast<uint4*>(bt + tc::swz_offset(t, c * 16, kN)) = hi;
+      *reinterpret_cast<uint4*>(bt + tc::swz_offset(4 + t, c * 16, kN)) = lo;
+    }
+  }
+  tc::fence_proxy_async_smem();
+  named_bar(kBarSplit, kNT);
+  if (sidx == 0) mbar_arrive(&aux.xb_ready);
 }
 
 // ---------------------------------------------------------------- the cluster kernel
@@ -425,26 +490,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (; ok && s_next < kFStages && s_next < n_total; ++s_next) ok = issue(s_next, 0, &msh13, &msh2);
       griddep_wait();
       griddep_launch();
-      // the route kernel left x split into the up MMAs' B operand: one bulk copy from L2
-      mbar_arrive_expect_tx(&aux.xb_ready, static_cast<uint32_t>(S.xb_bytes));
-      bulk_g2s(smem + S.xb, p.ws + L.ximg, static_cast<uint32_t>(S.xb_bytes), &aux.xb_ready);
     }
     __syncwarp();
-    named_bar(kBarTable, kThreads);
+    named_bar(kBarTable, kTableThreads);
     if (lane == 0) {
       if (slot < aux.n_slots) {
         const int ex = shared_slot ? 0 : aux.tab.expert[slot];
         const CUtensorMap* m13 = shared_slot ? &msh13 : &map13;
         const CUtensorMap* m2 = shared_slot ? &msh2 : &map2;
         for (; ok && s_next < n_total; ++s_next) ok = issue(s_next, ex, m13, m2);
-      } else if (!mbar_wait(&aux.xb_ready, 0)) {  // the copy lands before this idle CTA leaves
-        flag_error(p, L, STATUS_TIMEOUT);
       }
     }
     __syncwarp();
   } else if (warp == kWarpMma) {
     // ================================================================ MMA issuer (lane 0 issues)
-    named_bar(kBarTable, kThreads);
+    named_bar(kBarTable, kTableThreads);
     if (lane == 0 && slot < aux.n_slots) {
       bool ok = mbar_wait(&aux.xb_ready, 0);
       const uint32_t idesc = tc::idesc_e4m3(kTileRows, kN);
@@ -502,15 +562,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp < kWarpEpi) {
-    named_bar(kBarTable, kThreads);
+    // ================================================================ warps 2-3: the x split
+    griddep_wait();  // x comes from the preceding kernels
+    cl_split_x(p, smem + S.xb, aux, tid - 64);
   } else {
     // ================================================================ selection, then epilogues
     const int e = warp - kWarpEpi, et = tid - kWarpEpi * 32;
     griddep_wait();
     griddep_launch();
     {
-      // the logits of every row (the last column is the shared expert's gate) and x's split scale,
-      // requested at once: one L2 round trip
+      // the logits of every row (the last column is the shared expert's gate), requested at once:
+      // one L2 round trip
       const int rows = p.n_router + (p.sh_w13 != nullptr && p.sh_gate != nullptr ? 1 : 0);
       const float* lg = reinterpret_cast<const float*>(p.ws + L.logits);
       constexpr int kPer = (kMaxT * (kMaxRouter + 1) + kEpiThreads - 1) / kEpiThreads;
@@ -520,13 +582,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int k = et + i * kEpiThreads;
         v[i] = k < p.T * (kMaxRouter + 1) && k % (kMaxRouter + 1) < rows ? __ldcg(lg + k) : 0.f;
       }
-      const float xi = et < kMaxT ? __ldcg(reinterpret_cast<const float*>(p.ws + L.xinv) + et) : 1.f;
 #pragma unroll
       for (int i = 0; i < kPer; ++i) {
         const int k = et + i * kEpiThreads;
         if (k < kMaxT * (kMaxRouter + 1)) (&aux.rt.logits[0][0])[k] = v[i];
       }
-      if (et < kMaxT) aux.xinv[et] = xi;
     }
     named_bar(kBarEpi, kEpiThreads);
     if (e < p.T) route_row(p, aux.rt, e, lane, blockIdx.x == 0);
@@ -535,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = table_smem(p, aux.rt, lane, aux.tab);
       if (lane == 0) aux.n_slots = n;
     }
-    named_bar(kBarTable, kThreads);
+    named_bar(kBarTable, kTableThreads);
     if (slot < aux.n_slots) {
       const ExpertRef ex = expert_ref(p, slot, aux.tab.expert);
       const int r = 32 * e + lane;
@@ -552,7 +612,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       hold(sc13);
       hold(sc2);
-      bool ok = epi_wait_all(aux, &aux.acc_full, 0, false, e, lane);
+      // xb_ready orders the split warps' xinv before this read; acc_full comes later anyway
+      bool ok = epi_wait_all(aux, &aux.xb_ready, 0, false, e, lane);
+      ok = ok && epi_wait_all(aux, &aux.acc_full, 0, false, e, lane);
       if (ok) {
         tc::fence_after_sync();
         cl_epilogue_up(p, aux, smem + S.hb, tmem + tlane, shared_slot, q, e, lane, sc13);
@@ -574,10 +636,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar(kBarEpi, kEpiThreads);
         if (et == 0) {
           __threadfence();  // cumulative over the CTA's reductions, ordered by the barrier above
-          const uint32_t old = atomicAdd(ctrl(p, L) + CTRL_FCOUNT, 1u);
-          if (old == static_cast<uint32_t>(aux.n_slots * nq * kCl - 1)) {
+          // one count per half of the output rows: the two halves are converted by two CTAs
+          const uint32_t old = atomicAdd(ctrl(p, L) + CTRL_FCOUNT + q, 1u);
+          if (old == static_cast<uint32_t>(aux.n_slots * nq - 1)) {
             __threadfence();
-            ctrl(p, L)[CTRL_FCOUNT] = 0u;  // every CTA has counted: ready for the next call
+            ctrl(p, L)[CTRL_FCOUNT + q] = 0u;  // every CTA of this half has counted: ready for the next call
             aux.final_cta = 1;
           }
         }
@@ -591,5 +654,5 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == kWarpMma) tc::tmem_dealloc(tmem, kFTmemCols);
-  if (aux.final_cta) cl_finish(p, L, aux, tid);
+  if (aux.final_cta) cl_finish(p, L, aux, tid, q);
 }

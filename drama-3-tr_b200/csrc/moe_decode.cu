@@ -114,8 +114,8 @@ struct Params {
 struct WsLayout {
   size_t ctrl, slot_expert, coef, gate, logits, himg, himg_stride, hinv, ximg, xinv, partial, facc, total;
 };
-// CTRL_FCOUNT: CTAs of the cluster kernel that have added their partial sums (back at zero after
-// every call)
+// CTRL_FCOUNT + q: CTAs of the cluster kernel that have added their partial sums to output half q
+// (back at zero after every call)
 enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_FCOUNT = 6, CTRL_WORDS = 16 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -556,16 +556,19 @@ __global__ void __launch_bounds__(RW * kRouteSplit * 32) route_kernel(const __gr
         float m = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(__bfloat162float(e[i])));
-        // a warp's chunks lie in one row (H / 8 is a multiple of 32): one shared atomic per warp
-        const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
-        if (lane == 0) atomicMax(&rt.xmax[c / (H / 8)], wm);
+        // a warp's chunks lie in one row (H / 8 is a multiple of 32): one shared atomic per warp (the
+        // maxima only serve the x split, which the cluster kernel does itself)
+        if (!p.fused) {
+          const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+          if (lane == 0) atomicMax(&rt.xmax[c / (H / 8)], wm);
+        }
       }
     }
   }
   if (threadIdx.x == 0 && !mbar_wait(&rt.bar, 0)) flag_error(p, L, STATUS_TIMEOUT);
   __syncthreads();
   // this CTA's share of the x split: 16-element chunks c = blockIdx.x + gridDim.x * j
-  {
+  if (!p.fused) {
     uint8_t* img = p.ws + L.ximg;
     const int chunks = H / 16;
     for (int c = blockIdx.x + gridDim.x * static_cast<int>(threadIdx.x); c < p.T * chunks;
