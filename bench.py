@@ -416,7 +416,9 @@ def run_decode(args, world, rank, local, speaker=False):
             "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4),
             "peak_source": f"{pk['source']} HBM copy bandwidth",
-            "kernel": "one decode layer: dm3::moe route + up + down + combine kernels",
+            "kernel": ("one decode layer: dm3::moe route_kernel + layer_kernel (2-CTA clusters)"
+                       if os.environ.get("DM3_CLUSTER", "1") != "0"
+                       else "one decode layer: dm3::moe route + up + down + combine kernels"),
             "bytes_per_launch": round(bytes_step / n_layers),
             "traffic": recorded_traffic("moe_decode_layer"),
         },
