@@ -737,21 +737,21 @@ def run_prefill(args, world, rank, local):
 
 
 def run_gemv(args, world, rank, local):
-    """Block-FP8 GEMV sweep: per shape, 40 distinct weight copies in one graph (each launch reads
-    cold weights, as the reference's own timing rotates 40 layers, fp8_linear.py:82-103)."""
+    """Block-FP8 GEMV sweep: per shape and scale layout, 40 distinct weight copies in one graph (each
+    launch reads cold weights, as the reference's own timing rotates 40 layers, fp8_linear.py:82-103).
+    Layouts: 128x128 block scales (fp8_block, the layout the sweep is specified in) and 1x128 row
+    scales (fp8_linear.quantize). The audio head also runs as the gather kernel: 4,097 rows (eos + a
+    4,096-row band) taken from a seeded 252,000 x 2,048 block-FP8 matrix by an index list; the 40
+    copies use 40 band starts so that every launch reads rows L2 does not hold."""
+    import ctypes
     import drama3_b200 as dm3
 
     dev = torch.device("cuda", local)
     res = {}
     copies = 40
-    for (k, n) in [(2048, 4096), (4096, 2048), (2048, 8192), (2048, 512), (2048, 4097)]:
-        g = torch.Generator(device=dev).manual_seed(k + n)
-        ws = [dm3.quantize(torch.randn(n, k, generator=g, device=dev) * 0.02) for _ in range(copies)]
-        x = rms(torch.randn(2, k, generator=g, device=dev)).to(torch.bfloat16)
-        [dm3.ops.fp8_gemv(x, q, s) for q, s in ws]
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            ys = [dm3.ops.fp8_gemv(x, q, s) for q, s in ws]
+    hbm = peaks()["hbm_gbs"]
+
+    def timed(graph, n_calls):
         for _ in range(max(args.warmup, 3)):
             graph.replay()
         torch.cuda.synchronize()
@@ -761,17 +761,76 @@ def run_gemv(args, world, rank, local):
             graph.replay()
         e1.record()
         torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1000.0 / (args.steps * copies)
-        nbytes = n * k + n * (k // 128) * 4 + 2 * k * 2 + 2 * n * 2
-        res[f"{k}x{n}"] = {"us": round(us, 3), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
-                           "frac": round(nbytes / (us * 1e-6) / 1e9 / peaks()["hbm_gbs"], 4)}
-        del ws, ys, graph
-    main_key = "2048x4096"
+        return e0.elapsed_time(e1) * 1000.0 / (args.steps * n_calls)
+
+    def block_quant(w):
+        n = w.shape[0]
+        pad = (-n) % 128
+        q, sc = dm3.fp8_block(torch.nn.functional.pad(w, (0, 0, 0, pad)) if pad else w)
+        return q[:n].contiguous(), sc.contiguous()
+
+    for layout in ("128x128", "1x128"):
+        for (k, n) in [(2048, 4096), (4096, 2048), (2048, 8192), (2048, 512), (2048, 4097)]:
+            g = torch.Generator(device=dev).manual_seed(k + n)
+            quant = block_quant if layout == "128x128" else dm3.quantize
+            ws = [quant(torch.randn(n, k, generator=g, device=dev) * 0.02) for _ in range(copies)]
+            x = rms(torch.randn(2, k, generator=g, device=dev)).to(torch.bfloat16)
+            [dm3.ops.fp8_gemv(x, q, sc) for q, sc in ws]
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                ys = [dm3.ops.fp8_gemv(x, q, sc) for q, sc in ws]
+            us = timed(graph, copies)
+            sbytes = ws[0][1].numel() * 4
+            nbytes = n * k + sbytes + 2 * k * 2 + 2 * n * 2
+            res[f"{k}x{n}/{layout}"] = {"us": round(us, 3), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
+                                        "frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4)}
+            del ws, ys, graph
+            torch.cuda.empty_cache()
+
+    # audio head gathered in the kernel from the full-vocabulary matrix (128x128 scales)
+    V, K, NH = 252000, 2048, 4097
+    g = torch.Generator(device=dev).manual_seed(252000)
+    qf = torch.empty(V, K, dtype=torch.float8_e4m3fn, device=dev)
+    sf = torch.empty((V + 127) // 128, K // 128, dtype=torch.float32, device=dev)
+    for r0 in range(0, V, 16384):
+        r1 = min(V, r0 + 16384)
+        qb, sb = block_quant(torch.randn(r1 - r0, K, generator=g, device=dev) * 0.02)
+        qf[r0:r1] = qb
+        sf[r0 // 128:r0 // 128 + sb.shape[0]] = sb
+    x = rms(torch.randn(2, K, generator=g, device=dev)).to(torch.bfloat16)
+    starts = torch.randperm((V - 1 - NH) // 128, generator=g, device=dev)[:copies] * 128 + 1
+    idx = [torch.cat([torch.tensor([V - 1], device=dev), torch.arange(int(s0), int(s0) + NH - 1, device=dev)])
+           for s0 in starts.tolist()]
+    ys = [torch.empty(2, NH, dtype=torch.float32, device=dev) for _ in range(copies)]
+    lib = dm3._lib.load()
+
+    def head_calls():
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for rows, y in zip(idx, ys):
+            rc = lib.dm3_fp8_gemv_gather(ctypes.c_void_p(x.data_ptr()), 2, K, NH, ctypes.c_void_p(qf.data_ptr()), K, V,
+                                         ctypes.c_void_p(rows.data_ptr()), ctypes.c_void_p(sf.data_ptr()), K // 128,
+                                         128, ctypes.c_void_p(y.data_ptr()), NH, 1, st)
+            assert rc == 0, lib.dm3_last_error()
+
+    head_calls()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        head_calls()
+    us = timed(graph, copies)
+    nbytes = NH * K + NH * (K // 128) * 4 + NH * 8 + 2 * K * 2 + 2 * NH * 4
+    res["2048x4097/128x128/gathered"] = {"us": round(us, 3), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1),
+                                         "frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4)}
+    del qf, sf, graph
+    main_key = "2048x4096/128x128"
     return {"metric": "block-FP8 GEMV (M=2) per call", "value": res[main_key]["us"], "unit": "us/call",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 x bf16", "data": "synthetic",
-            "config": {"workload": "gemv_sweep_m2_1x128", "copies": copies}, "shapes": res,
-            "gpu_launches": args.steps * copies}
+            "config": {"workload": "gemv_sweep_m2", "copies": copies, "value_shape": main_key,
+                       "l2": "no flush: 40 distinct weight copies per graph, each launch reads cold rows"},
+            "roofline": {"bound": "hbm", "achieved": res[main_key]["GBps"], "peak": hbm, "unit": "GB/s",
+                         "frac": res[main_key]["frac"], "kernel": "dm3::gemv_tc::gemv_tc_kernel, 2048x4096",
+                         "traffic": None},
+            "shapes": res, "gpu_launches": args.steps * copies * 11}
 
 
 def run_reference_prefill(args, world):
