@@ -362,12 +362,8 @@ __device__ __forceinline__ void warp_top8_32(uint32_t (&k)[8]) {
 __device__ void route_row(const Params& p, RouteTail& rt, int t, int lane, bool emit = true) {
   const int E = p.n_router, K = p.top_k;
   float lv[8];
-  float mloc = -FLT_MAX;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    lv[i] = lane + 32 * i < E ? rt.logits[t][lane + 32 * i] : -FLT_MAX;
-    mloc = fmaxf(mloc, lv[i]);
-  }
+  for (int i = 0; i < 8; ++i) lv[i] = lane + 32 * i < E ? rt.logits[t][lane + 32 * i] : -FLT_MAX;
   int sel_e[8];
   float sel_v[8];
   if (p.logits_bf16 && p.logit_bias == nullptr) {
@@ -398,10 +394,9 @@ __device__ void route_row(const Params& p, RouteTail& rt, int t, int lane, bool 
       sel_v[j] = key_value(static_cast<uint32_t>(k[j] >> 32));
     }
   }
-  // softmax denominator (the maximum by its own butterfly, so it overlaps the selection)
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, o));
-  const float m = mloc;
+  // softmax denominator; the maximum logit is the first selection's value (every lane holds the
+  // merged top 8)
+  const float m = sel_v[0];
   float z = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
