@@ -1,8 +1,8 @@
 // Decode MoE layer for B200 (sm_100a) as four chained kernels, each launched with programmatic
 // dependent launch so that a kernel's constant-weight loads start while its predecessor finishes:
 //
-//   route    router logits (exact products, summed in a hi + lo pair and rounded once), one warp
-//            per router row
+//   route    router logits (exact products, summed in fp64 and rounded once), four warps per
+//            router row
 //   up       gate and up rows of every selected expert (+ the shared expert) on the tensor cores:
 //            items of 64 gate + the matching 64 up rows over all of H; SwiGLU in the epilogue;
 //            h written as bf16
@@ -318,7 +318,7 @@ struct RouteTail {
   uint64_t bar;
   int last;
   uint32_t xmax[kMaxT];
-  float2 part[kRouteWarps][kMaxT][kRouteSplit];  // (hi, lo) of each warp's quarter of a row
+  double part[kRouteWarps][kMaxT][kRouteSplit];  // fp64 sum of each warp's quarter of a row
   float logits[kMaxT][kMaxRouter + 1];
   int sel_e[kMaxT * kMaxTopK];
   float sel_w[kMaxT * kMaxTopK];
@@ -467,15 +467,6 @@ __device__ void write_table(const Params& p, const WsLayout& L, RouteTail& rt, i
   if (lane == 0) ctrl(p, L)[CTRL_NSLOTS] = static_cast<uint32_t>(base + total);
 }
 
-// Adds a to the unevaluated sum hi + lo without rounding error in hi (Knuth's TwoSum; the error
-// term goes to lo).
-__device__ __forceinline__ void two_sum_acc(float& hi, float& lo, float a) {
-  const float s = hi + a;
-  const float bb = s - hi;
-  lo += (hi - (s - bb)) + (a - bb);
-  hi = s;
-}
-
 // Shared memory of the route kernel: the CTA's router rows (staged by bulk copies before the
 // wait), the activation rows, then RouteTail.
 // rw router rows per CTA, T activation rows.
@@ -491,10 +482,10 @@ __host__ __device__ inline size_t route_smem_bytes(int H, bool w32, int rw, int 
 // Router logits, then the route table. Four warps per router row (plus the shared expert's gate
 // row), each summing a quarter of H. The CTA's rows are copied into shared memory by the bulk-copy
 // engine before griddepcontrol.wait (router weights never depend on the preceding kernel); the
-// activation rows are staged after it. Every product is exact in fp32 (bf16 x bf16; bf16 x fp32
-// keeps its rounding error through an fma) and is summed as a hi + lo pair, which carries about 48
-// significant bits, so the logit is the sum rounded once to fp32 (then to bf16 for a bf16 router),
-// + the optional logit bias. The shared gate row is rounded to bf16 as a bf16 linear's output.
+// activation rows are staged after it. Every product is exact in fp64 (bf16 x bf16 or bf16 x fp32)
+// and the products are summed in fp64, so the logit is the sum rounded once to fp32 (then to bf16
+// for a bf16 router), + the optional logit bias. (Summing in fp64 replaced an fp32 hi + lo pair
+// with the same precision for this purpose: its dependent chains were about 1 µs longer.) The shared gate row is rounded to bf16 as a bf16 linear's output.
 // Each CTA also splits its share of x into the up kernel's activation tile (the exact e4m3 hi / lo
 // of x * 2^e per row). The last CTA to finish (one gpu-scope fence per CTA, with no copies in
 // flight) selects the experts of every row (one warp per row) and writes the table.
@@ -585,7 +576,7 @@ __global__ void __launch_bounds__(RW * kRouteSplit * 32) route_kernel(const __gr
     const int k0 = quarter * (H / kRouteSplit), k1 = k0 + H / kRouteSplit;
     for (int t = 0; t < p.T; ++t) {
       const __nv_bfloat16* xr = xs + t * H;
-      float hi[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, lo[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      double acc[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll 1
       for (int k = k0 + lane * 8; k < k1; k += 256) {
         const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
@@ -601,40 +592,25 @@ __global__ void __launch_bounds__(RW * kRouteSplit * 32) route_kernel(const __gr
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[i] = __bfloat162float(we[i]);
         }
+        // each product is exact in fp64 (bf16 x bf16 or bf16 x fp32), added with one rounding
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float xf = __bfloat162float(xe[i]);
-          const float pr = xf * w[i];
-          if (W32) lo[i] += fmaf(xf, w[i], -pr);  // the product's rounding error, exact (0 for bf16 x bf16)
-          two_sum_acc(hi[i], lo[i], pr);
-        }
+        for (int i = 0; i < 8; ++i)
+          acc[i & 3] = fma(static_cast<double>(__bfloat162float(xe[i])), static_cast<double>(w[i]), acc[i & 3]);
       }
-      float h = hi[0], l = lo[0];
+      double sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
 #pragma unroll
-      for (int i = 1; i < 8; ++i) {
-        l += lo[i];
-        two_sum_acc(h, l, hi[i]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float oh = __shfl_xor_sync(0xffffffffu, h, o);
-        l += __shfl_xor_sync(0xffffffffu, l, o);
-        two_sum_acc(h, l, oh);
-      }
-      if (lane == 0) rt.part[rw][t][quarter] = make_float2(h, l);
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) rt.part[rw][t][quarter] = sum;
     }
   }
   __syncthreads();
   if (threadIdx.x < RW * kMaxT) {
     const int r = threadIdx.x / kMaxT, t = threadIdx.x % kMaxT;
     if (row0 + r < rows && t < p.T) {
-      float h = rt.part[r][t][0].x, l = rt.part[r][t][0].y;
+      double sum = rt.part[r][t][0];
 #pragma unroll
-      for (int q = 1; q < kRouteSplit; ++q) {
-        l += rt.part[r][t][q].y;
-        two_sum_acc(h, l, rt.part[r][t][q].x);
-      }
-      float v = h + l;
+      for (int q = 1; q < kRouteSplit; ++q) sum += rt.part[r][t][q];
+      float v = __double2float_rn(sum);  // the logit rounded once
       if (row0 + r < p.n_router) {
         if (p.logits_bf16) v = bf16_round(v);
         if (p.logit_bias) v += p.logit_bias[row0 + r];
