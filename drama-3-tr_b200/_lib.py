@@ -26,6 +26,8 @@ SIGNATURES = {
     "dm3_version": (ctypes.c_char_p, []),
     "dm3_fp8_gemv": (_i, [_p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p, _i, _p, _i64, _i, _p]),
     "dm3_fp8_gemv_gather": (_i, [_p, _i, _i, _i, _p, _i64, _i64, _p, _p, _i64, _i, _p, _i64, _i, _p]),
+    "dm3_fp8_gemm_workspace_bytes": (_sz, [_i, _i]),
+    "dm3_fp8_gemm": (_i, [_p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p, _i, _p, _i64, _i, _p, _sz, _p]),
     "dm3_moe_workspace_bytes": (_sz, [_i, _i, _i]),
     "dm3_moe_forward": (_i, [_p, _i, _i, _i, _p, _p, _i, _i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p,
                              _sz, _p]),
@@ -34,6 +36,8 @@ SIGNATURES = {
     "dm3_moe_status": (_i, [_p, _u32p, _p]),
     "dm3_moe_layer_noalloc": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i,
                                    _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p]),
+    "dm3_moe_noalloc_status": (_i, [_u32p, _p]),
+    "dm3_set_wait_limit_ns": (_i, [ctypes.c_uint64]),
     "dm3_moe_prefill_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "dm3_moe_prefill": (_i, [_p, _i, _i, _i, _p, _i, _i, _i, _p, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _p, _p,
                              _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p]),

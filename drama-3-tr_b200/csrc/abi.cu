@@ -130,3 +130,16 @@ extern "C" const char* dm3_last_error(void) { return dm3::g_error.c_str(); }
 extern "C" const char* dm3_version(void) { return "0.1.0"; }
 
 extern "C" int dm3_last_launch_count(void) { return dm3::g_launches; }
+
+extern "C" int dm3_set_wait_limit_ns(uint64_t ns) {
+  if (ns == 0) return dm3::set_error("the wait limit must be at least 1 ns"), 1;
+  int (*setters[])(uint64_t) = {dm3::wait_limit_gemm, dm3::wait_limit_gemv, dm3::wait_limit_gemv_tc, dm3::wait_limit_moe_decode,
+                                dm3::wait_limit_moe_prefill};
+  for (auto fn : setters) {
+    const int err = fn(ns);
+    if (err != 0)
+      return dm3::set_error(std::string("setting the wait limit: ") +
+                            cudaGetErrorString(static_cast<cudaError_t>(err))), 2;
+  }
+  return 0;
+}

@@ -24,8 +24,15 @@ enum : uint32_t {
   STATUS_BAD_EXPERT = 2u,   // an expert id outside [0, n_experts) was skipped
 };
 
-// Upper bound of every spin in these kernels (nanoseconds of %globaltimer).
-constexpr uint64_t kWaitLimitNs = 1000000000ull;
+// Upper bound of every spin in these kernels, in nanoseconds of %globaltimer: 1 s unless
+// dm3_set_wait_limit_ns changed it on the device. Each translation unit holds its own copy (a
+// static device variable), which set_wait_limit_here writes on the current device.
+constexpr uint64_t kDefaultWaitLimitNs = 1000000000ull;
+static __device__ uint64_t g_wait_limit_ns = kDefaultWaitLimitNs;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return g_wait_limit_ns; }
+static inline cudaError_t set_wait_limit_here(uint64_t ns) {
+  return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+}
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -80,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) 
   if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait_sleep(bar, parity, 100000u)) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > wait_limit_ns()) return false;
   }
   return true;
 }
@@ -89,7 +96,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > wait_limit_ns()) return false;
   }
   return true;
 }
@@ -131,7 +138,7 @@ __device__ __forceinline__ bool wait_geq(const uint32_t* p, uint32_t target) {
   if (ld_acquire(p) >= target) return true;
   const uint64_t t0 = globaltimer();
   while (ld_acquire(p) < target) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > wait_limit_ns()) return false;
     __nanosleep(64);
   }
   return true;

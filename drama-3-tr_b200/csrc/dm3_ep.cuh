@@ -69,7 +69,7 @@ __device__ __forceinline__ bool wait_epoch(const uint32_t* flagp, uint32_t epoch
   if (ld_acquire_sys(flagp) == epoch) return true;
   const uint64_t t0 = globaltimer();
   while (ld_acquire_sys(flagp) != epoch) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > wait_limit_ns()) return false;
     __nanosleep(100);
   }
   return true;

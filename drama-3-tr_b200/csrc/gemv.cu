@@ -375,3 +375,8 @@ extern "C" int dm3_fp8_gemv_gather(const void* x, int M, int K, int N, const voi
                           rows, n_rows_q, s, lds, srows, nullptr, 0, y, ldy, y_fp32,
                           static_cast<cudaStream_t>(stream));
 }
+
+namespace dm3 {
+// This file's copy of the device wait limit on the current device (dm3_set_wait_limit_ns).
+int wait_limit_gemv(uint64_t ns) { return static_cast<int>(set_wait_limit_here(ns)); }
+}  // namespace dm3

@@ -306,3 +306,8 @@ int launch_gemv_tc(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q
 }
 
 }  // namespace dm3
+
+namespace dm3 {
+// This file's copy of the device wait limit on the current device (dm3_set_wait_limit_ns).
+int wait_limit_gemv_tc(uint64_t ns) { return static_cast<int>(set_wait_limit_here(ns)); }
+}  // namespace dm3

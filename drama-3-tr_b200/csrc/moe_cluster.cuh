@@ -130,7 +130,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait_cluster(bar, parity)) {
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > wait_limit_ns()) return false;
   }
   return true;
 }

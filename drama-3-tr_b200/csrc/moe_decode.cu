@@ -29,9 +29,12 @@
 // Ordering under programmatic dependent launch: every kernel calls griddepcontrol.launch_dependents
 // only after its own griddepcontrol.wait, so once a kernel is running, everything two launches
 // back has completed. The down kernel relies on that to select experts before its wait.
+#include <atomic>
 #include <cfloat>
 #include <cstddef>
 #include <cmath>
+#include <mutex>
+#include <string>
 #include <utility>
 
 #include "dm3_common.cuh"
@@ -1531,8 +1534,31 @@ namespace {
 
 constexpr size_t kNoAllocScratchBytes = 1572864;  // 1.5 MiB: the workspace of H <= 2048, I <= 512
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
-// Device address of g_noalloc_scratch per device; the host-side symbol is not a device address.
-void* g_noalloc_ptr[64] = {nullptr};
+// Device address of g_noalloc_scratch per device (the host-side symbol is not a device address),
+// published once the array has been zeroed on that device.
+std::atomic<void*> g_noalloc_ptr[64];
+std::mutex g_noalloc_mu;
+
+// The array's device address on device `dev` (current), zeroing it on the first call there: the
+// memset is waited for before the address is published, so no caller can launch on a half-cleared
+// array. Null (with the error set) when the runtime refuses, e.g. during stream capture.
+void* noalloc_scratch(int dev, cudaStream_t stream) {
+  void* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (ptr != nullptr) return ptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  ptr = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+  if (ptr != nullptr) return ptr;
+  cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (err != cudaSuccess) return dm3::set_error(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(err)), nullptr;
+  err = cudaMemsetAsync(ptr, 0, kNoAllocScratchBytes, stream);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+  if (err != cudaSuccess)
+    return dm3::set_error(std::string("clearing the static scratch (make the first call outside stream capture): ") +
+                          cudaGetErrorString(err)),
+           nullptr;
+  g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+  return ptr;
+}
 
 }  // namespace
 
@@ -1544,22 +1570,41 @@ extern "C" int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const v
                                      int sh_srows, const void* sh_gate, const float* out_bias, void* y,
                                      int64_t* ids_out, void* w_out, void* stream) {
   dm3::note_launches(0);
-  if (H > 0 && I > 0 && H <= dm3::kMaxH && I <= dm3::kMaxI &&
-      dm3::moe_ws_bytes(H, I) > kNoAllocScratchBytes)
-    return dm3::set_error("H and I need more scratch than the 1.5 MiB static array holds"), 4;
+  if (H > dm3::kMaxH || I > dm3::kMaxI || (H > 0 && I > 0 && dm3::moe_ws_bytes(H, I) > kNoAllocScratchBytes))
+    return dm3::set_error("the static 1.5 MiB scratch holds the layer of H <= 2048 and I <= 512 only"), 4;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return dm3::set_error("no usable current CUDA device"), 2;
-  if (g_noalloc_ptr[dev] == nullptr) {
-    // first call on this device: look up the array's device address and zero it once
-    void* ptr = nullptr;
-    cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (err != cudaSuccess) return dm3::set_error(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(err)), 2;
-    err = cudaMemsetAsync(ptr, 0, kNoAllocScratchBytes, static_cast<cudaStream_t>(stream));
-    if (err != cudaSuccess) return dm3::set_error(std::string("clearing the static scratch: ") + cudaGetErrorString(err)), 2;
-    g_noalloc_ptr[dev] = ptr;
-  }
+  void* scratch = noalloc_scratch(dev, static_cast<cudaStream_t>(stream));
+  if (scratch == nullptr) return 2;
   return dm3_moe_layer(x, T, H, I, router_w, router_dtype, n_router, top_k, logits_bf16, logit_bias, w13, w13_stride,
                        s13, s13_stride, w2, w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows,
-                       sh_gate, out_bias, y, ids_out, w_out, g_noalloc_ptr[dev], kNoAllocScratchBytes, stream);
+                       sh_gate, out_bias, y, ids_out, w_out, scratch, kNoAllocScratchBytes, stream);
 }
+
+extern "C" int dm3_moe_noalloc_status(uint32_t* status, void* stream) {
+  if (!status) return dm3::set_error("null pointer argument"), 1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return dm3::set_error("no usable current CUDA device"), 2;
+  *status = 0;
+  void* scratch = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (scratch == nullptr) return 0;  // no call has run on this device yet
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* word = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(scratch) + dm3::moe::ws_layout(128, 128).ctrl) +
+                   dm3::moe::CTRL_STATUS;
+  uint32_t v = 0;
+  if (cudaMemcpyAsync(&v, word, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)
+    return dm3::set_error("reading the static scratch's status failed"), 2;
+  // a call that stopped early may have left counters and partial sums behind: clear the whole array
+  if (v != 0 && (cudaMemsetAsync(scratch, 0, kNoAllocScratchBytes, s) != cudaSuccess ||
+                 cudaStreamSynchronize(s) != cudaSuccess))
+    return dm3::set_error("clearing the static scratch failed"), 2;
+  *status = v;
+  return (v & dm3::STATUS_TIMEOUT) ? 3 : 0;
+}
+
+namespace dm3 {
+// This file's copy of the device wait limit on the current device (dm3_set_wait_limit_ns).
+int wait_limit_moe_decode(uint64_t ns) { return static_cast<int>(set_wait_limit_here(ns)); }
+}  // namespace dm3

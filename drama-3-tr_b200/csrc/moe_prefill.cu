@@ -1830,3 +1830,8 @@ extern "C" int dm3_ep_combine(const void* x, int T, int H, int I, const void* ro
                     w2_stride, s2, s2_stride, srows, sh_w13, sh_s13, sh_w2, sh_s2, sh_srows, sh_gate, out_bias, y,
                     nullptr, nullptr, world, rank, tokens_per_rank, arenas, nullptr, workspace, workspace_bytes, stream);
 }
+
+namespace dm3 {
+// This file's copy of the device wait limit on the current device (dm3_set_wait_limit_ns).
+int wait_limit_moe_prefill(uint64_t ns) { return static_cast<int>(set_wait_limit_here(ns)); }
+}  // namespace dm3

@@ -7,6 +7,7 @@ node. There is no fallback: a missing library or a non-CUDA tensor raises.
 
 Ops:
   dm3::fp8_gemv      block-FP8 GEMV, <= 4 rows per launch (fp8_linear.py:10-27 `_gemv`)
+  dm3::fp8_gemm      block-FP8 GEMM for more rows (fp8_linear.py:60-61 dequantise + F.linear)
   dm3::moe_forward   grouped SwiGLU over block-FP8 experts with given routing
                      (fish-speech fp8_moe_forward, engine.py:147, :236)
   dm3::moe_layer     fused decode MoE layer: router + top-k + experts + shared expert + bias
@@ -145,6 +146,65 @@ def fp8_gemv(x: Tensor, q: Tensor, s: Tensor, bias: Optional[Tensor] = None, out
 
 
 @fp8_gemv.register_fake
+def _(x, q, s, bias=None, out_fp32=False):
+    return x.new_empty((x.shape[0], q.shape[0]), dtype=torch.float32 if out_fp32 else BF16)
+
+
+# ----------------------------------------------------------------------------- fp8_gemm
+_gemm_workspaces: dict = {}
+
+
+def gemm_workspace(device: torch.device, nbytes: int) -> Tensor:
+    """The zero-initialised scratch of the block-FP8 GEMM on one device (activation image, token
+    exponents, status word), grown on demand and shared by calls issued in stream order."""
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _gemm_workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("drama3_b200: the GEMM workspace must be created before CUDA-graph capture; run "
+                               "the op once at the largest row count first")
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _gemm_workspaces[key] = ws
+    return ws
+
+
+@torch.library.custom_op("dm3::fp8_gemm", mutates_args=())
+def fp8_gemm(x: Tensor, q: Tensor, s: Tensor, bias: Optional[Tensor] = None, out_fp32: bool = False) -> Tensor:
+    """y[M, N] = x[M, K] @ dequant(q[N, K], s).T (+ bias) for any row count: the block-FP8 GEMM on
+    the tensor cores (where the reference dequantises and calls F.linear, fp8_linear.py:60-61).
+
+    x bf16 [M, K]; q e4m3 [N, K] with unit column stride; s fp32 [N, K/128] (1x128) or
+    [ceil(N/128), K/128] (128x128)."""
+    _require_cuda(x, q, s, bias)
+    lib = _lib.load()
+    q = _fp8_bytes(q)
+    if x.dtype != BF16:
+        raise RuntimeError("fp8_gemm expects bf16 activations")
+    x = x.contiguous()
+    s = s.contiguous()
+    M, K = x.shape
+    N = q.shape[0]
+    if q.stride(1) != 1 or q.shape[1] != K:
+        raise RuntimeError("q must be [N, K] with unit column stride")
+    srows = scale_rows(N, s.shape[0])
+    y = torch.empty((M, N), dtype=torch.float32 if out_fp32 else BF16, device=x.device)
+    bias_kind = 0
+    if bias is not None:
+        if bias.dtype not in (BF16, torch.float32):
+            bias = bias.float()
+        bias = bias.contiguous()
+        bias_kind = 1 if bias.dtype == BF16 else 2
+    if M == 0:
+        return y
+    ws = gemm_workspace(x.device, lib.dm3_fp8_gemm_workspace_bytes(M, K))
+    rc = lib.dm3_fp8_gemm(_ptr(x), M, K, N, _ptr(q), q.stride(0), _ptr(s), s.stride(0), srows, _ptr(bias), bias_kind,
+                          _ptr(y), N, 1 if out_fp32 else 0, _ptr(ws), ws.numel(), _stream(x.device))
+    _lib.check(rc, "dm3_fp8_gemm")
+    return y
+
+
+@fp8_gemm.register_fake
 def _(x, q, s, bias=None, out_fp32=False):
     return x.new_empty((x.shape[0], q.shape[0]), dtype=torch.float32 if out_fp32 else BF16)
 
@@ -348,3 +408,20 @@ def route(x: Tensor, router_w: Tensor, top_k: int, logits_bf16: bool,
 def _(x, router_w, top_k, logits_bf16, logit_bias):
     T = x.shape[0]
     return x.new_empty((T, top_k), dtype=torch.int64), x.new_empty((T, top_k), dtype=BF16)
+
+
+def set_wait_limit(ns: int) -> None:
+    """Time limit (nanoseconds) of every bounded device-side wait on the current device; 1 s by
+    default. A wait that runs out sets the timeout bit of the status word (moe_status) and the
+    kernel stops its work. Call while no kernel of the library runs on the device."""
+    _lib.check(_lib.load().dm3_set_wait_limit_ns(int(ns)), "dm3_set_wait_limit_ns")
+
+
+def noalloc_status() -> int:
+    """Status word of the allocation-free layer's static scratch on the current device (synchronises);
+    a non-zero word also clears the scratch so that the next call starts clean."""
+    st = ctypes.c_uint32(0)
+    rc = _lib.load().dm3_moe_noalloc_status(ctypes.byref(st), _stream(torch.device("cuda", torch.cuda.current_device())))
+    if rc not in (_lib.DM3_OK, _lib.DM3_ETIMEOUT):
+        _lib.check(rc, "dm3_moe_noalloc_status")
+    return int(st.value)

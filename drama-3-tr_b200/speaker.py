@@ -1,31 +1,44 @@
 """Drop-ins for the Drama-3 speaker pieces of the reference engine (engine.py:150-257).
 
-  fp8_block        128x128 block quantiser (engine.py:214-219)
-  Speaker          distilled top-k MoE for decode rows (engine.py:222-237), one fused launch
-  load_speaker     speaker checkpoint reader (engine.py:240-250)
-  attach_speaker   installs a Speaker per layer (engine.py:253-257)
-  speaker_forward  SparseMoeBlock.forward for decode rows (engine.py:153-158): the speaker, the
-                   shared expert and its sigmoid gate fused into one launch when the shared
-                   expert's linears are block-FP8 (the TTS_FP8 configuration, engine.py:201-206)
-  install          patches a loaded reference `engine` module to use all of the above
+  fp8_block          128x128 block quantiser (engine.py:214-219); byte-identical output
+  Speaker            distilled top-k MoE for decode rows (engine.py:222-237), one fused launch
+  read_speaker_file  reader of the speaker checkpoint written by release/convert_weights.py
+                     (`layers.{i}.{selected,gate,bias,w13,s13,w2,s2}`) or of the .pt list
+  speakers_from_file kernel-ready Speaker objects, one per layer, straight from such a file
+  speaker_forward    SparseMoeBlock.forward for decode rows (engine.py:153-158): the speaker, the
+                     shared expert and its sigmoid gate fused into one launch when the shared
+                     expert's linears are block-FP8 (the TTS_FP8 configuration, engine.py:201-206)
+  install            points a loaded reference `engine` module at all of the above
+
+The reference's own load_speaker / attach_speaker (engine.py:240-257) look up `Speaker` in their
+module, so after `install(engine)` they build these Speaker objects without being replaced.
 """
 
 from __future__ import annotations
+
+import re
+from pathlib import Path
+from typing import Dict, List, Optional
 
 import torch
 
 from . import ops
 
 BF16 = torch.bfloat16
+FP8 = torch.float8_e4m3fn
+
+# tensors of one speaker layer in the release file (release/convert_weights.py:14-18)
+SPEAKER_TENSORS = ("selected", "gate", "bias", "w13", "s13", "w2", "s2")
+_SPEAKER_KEY = re.compile(r"layers\.(\d+)\.(\w+)")
 
 
 def fp8_block(w: torch.Tensor):
-    """Block quantiser of engine.fp8_block: one fp32 scale = absmax/448 (clamped at 1e-12) per
-    128x128 block of the last two dims; q = e4m3(w / scale)."""
-    *lead, r, c = w.shape
-    b = w.float().view(*lead, r // 128, 128, c // 128, 128)
-    scale = b.abs().amax(dim=(-3, -1)).clamp(min=1e-12) / 448.0
-    q = (b / scale[..., :, None, :, None]).view(*lead, r, c).to(torch.float8_e4m3fn)
+    """e4m3 q and fp32 scales with one scale = max(absmax, 1e-12) / 448 per 128x128 block of the
+    last two dims, scales shaped [..., R / 128, C / 128]."""
+    *lead, rows, cols = w.shape
+    tiles = w.float().reshape(*lead, rows // 128, 128, cols // 128, 128)
+    scale = tiles.abs().amax(dim=(-3, -1)).clamp(min=1e-12) / 448.0
+    q = (tiles / scale.unsqueeze(-1).unsqueeze(-3)).reshape(*lead, rows, cols).to(FP8)
     return q, scale.float()
 
 
@@ -33,22 +46,28 @@ class Speaker:
     """The distilled speaker MoE of one layer: fp32 router [E, H], fp32 bias [H], block-FP8 experts.
 
     __call__(x) = (fp8_moe_forward(x, top-k routing of softmax(x.float() @ gate.T)) + bias).bf16,
-    computed by one dm3::moe_layer launch per 4 rows (engine.py:232-237)."""
+    computed by one dm3::moe_layer launch per 4 rows (engine.py:232-237). `p` holds gate, bias and
+    either the quantised experts (w13, s13, w2, s2) or bf16 / fp32 w13 and w2, which are quantised
+    here with fp8_block."""
 
     top_k = 8
 
-    def __init__(self, p: dict, device="cuda"):
-        self.gate = p["gate"].to(device).float().contiguous()
-        self.bias = p["bias"].to(device).float().contiguous()
-        if "s13" in p:
-            self.w13, self.s13, self.w2, self.s2 = (p[k].to(device) for k in ("w13", "s13", "w2", "s2"))
+    def __init__(self, p: Dict[str, torch.Tensor], device="cuda"):
+        dev = torch.device(device)
+        self.gate = p["gate"].to(device=dev, dtype=torch.float32).contiguous()
+        self.bias = p["bias"].to(device=dev, dtype=torch.float32).contiguous()
+        w13, w2 = p["w13"].to(dev), p["w2"].to(dev)
+        if "s13" in p and "s2" in p:
+            as_fp8 = lambda t: t.view(FP8) if t.dtype == torch.uint8 else t  # noqa: E731
+            self.w13, self.w2 = as_fp8(w13), as_fp8(w2)
+            self.s13, self.s2 = p["s13"].to(dev).float(), p["s2"].to(dev).float()
         else:
-            self.w13, self.s13 = fp8_block(p["w13"].to(device))
-            self.w2, self.s2 = fp8_block(p["w2"].to(device))
-        H, I = self.w13.shape[2], self.w13.shape[1] // 2
-        ops.moe_workspace(self.gate.device, H, I)  # created now so CUDA-graph capture never allocates it
+            self.w13, self.s13 = fp8_block(w13)
+            self.w2, self.s2 = fp8_block(w2)
+        hidden, inter = self.w13.shape[2], self.w13.shape[1] // 2
+        ops.moe_workspace(dev, hidden, inter)  # created now so CUDA-graph capture never allocates it
 
-    def route_and_combine(self, x: torch.Tensor, shared=None):
+    def route_and_combine(self, x: torch.Tensor, shared: Optional["SharedExpert"] = None):
         sh = shared.tensors() if shared is not None else (None, None, None, None, None)
         return ops.moe_layer(x, self.gate, self.top_k, False, None, self.w13, self.s13, self.w2, self.s2, *sh,
                              self.bias)
@@ -86,27 +105,31 @@ class SharedExpert:
         return SharedExpert(torch.cat([g.q, u.q]), torch.cat([g.s, u.s]), d.q, d.s, gate_row)
 
 
-def load_speaker(path):
-    """Per-layer speaker tensors from a .pt list or a safetensors file keyed
-    `layers.{i}.{selected,gate,bias,w13,s13,w2,s2}` (engine.py:240-250)."""
-    if not str(path).endswith(".safetensors"):
-        return torch.load(path, mmap=True)
-    from safetensors.torch import load_file
+def read_speaker_file(path) -> List[Dict[str, torch.Tensor]]:
+    """Per-layer speaker tensors (CPU) of a release safetensors file, or the list stored in a .pt file.
 
-    flat, layers = load_file(path), []
-    for key, t in flat.items():
-        i, name = key.split(".", 2)[1:]
-        layers += [{} for _ in range(int(i) + 1 - len(layers))]
-        layers[int(i)][name] = t
-    return layers
+    The safetensors keys are `layers.{i}.{name}` with name in SPEAKER_TENSORS; layers must be
+    numbered 0..L-1 without gaps. Raises ValueError on any other key."""
+    path = Path(path)
+    if path.suffix != ".safetensors":
+        return list(torch.load(path, mmap=True))
+    from safetensors import safe_open
+
+    per_layer: Dict[int, Dict[str, torch.Tensor]] = {}
+    with safe_open(str(path), framework="pt") as f:
+        for key in f.keys():
+            m = _SPEAKER_KEY.fullmatch(key)
+            if m is None or m.group(2) not in SPEAKER_TENSORS:
+                raise ValueError(f"{path}: unexpected tensor {key!r} in a speaker file")
+            per_layer.setdefault(int(m.group(1)), {})[m.group(2)] = f.get_tensor(key)
+    if sorted(per_layer) != list(range(len(per_layer))):
+        raise ValueError(f"{path}: layers {sorted(per_layer)} are not numbered 0..{len(per_layer) - 1}")
+    return [per_layer[i] for i in range(len(per_layer))]
 
 
-def attach_speaker(model, path):
-    """One Speaker per decoder layer (engine.py:253-257)."""
-    for layer, p in zip(model.backbone.model.layers, load_speaker(path)):
-        layer.mlp.experts.speaker = Speaker(p)
-        if "reader" in p:
-            layer.mlp.experts.reader = Speaker(p["reader"])
+def speakers_from_file(path, device="cuda") -> List[Speaker]:
+    """One kernel-ready Speaker per layer of a speaker file, tensors moved to `device`."""
+    return [Speaker(p, device=device) for p in read_speaker_file(path)]
 
 
 def make_speaker_forward(routed_forward, batch):
@@ -138,15 +161,14 @@ def make_speaker_forward(routed_forward, batch):
 
 def install(engine) -> None:
     """Points a loaded reference `engine` module at the B200 kernels: fp8_moe_forward (used by
-    OnDemandExperts.forward), Speaker, fp8_block, load/attach_speaker and the patched
-    SparseMoeBlock.forward. FP8 dense layers come from `drama3_b200.fp8_linear.convert`."""
+    OnDemandExperts.forward), Speaker and fp8_block (so the engine's own load_speaker /
+    attach_speaker build fused speakers), and the patched SparseMoeBlock.forward. FP8 dense layers
+    come from `drama3_b200.fp8_linear.convert`."""
     from . import fp8_moe
 
     engine.fp8_moe_forward = fp8_moe.fp8_moe_forward
     engine.fp8_block = fp8_block
     engine.Speaker = Speaker
-    engine.load_speaker = load_speaker
-    engine.attach_speaker = attach_speaker
     fwd = make_speaker_forward(engine.routed_forward, lambda: engine.OnDemandExperts.batch)
     engine.speaker_forward = fwd
     engine.SparseMoeBlock.forward = fwd

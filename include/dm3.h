@@ -73,6 +73,24 @@ int dm3_fp8_gemv_gather(const void* x, int M, int K, int N, const void* q, int64
                         const int64_t* rows, const float* s, int64_t lds, int srows, void* y, int64_t ldy,
                         int y_fp32, void* stream);
 
+/* Workspace bytes of dm3_fp8_gemm for M activation rows of K elements. */
+size_t dm3_fp8_gemm_workspace_bytes(int M, int K);
+
+/*
+ * Block-FP8 GEMM for any number of activation rows: y[m, n] = sum_k x[m, k] * float(q[n, k]) *
+ * s[n / srows, k / 128] (+ bias[n]) on the tensor cores, products exact and each 128-wide k block
+ * scaled in fp32. Replaces FP8Linear.forward's path for more than 2 rows, which dequantises the
+ * weight and calls F.linear (fp8_linear.py:60-61), as the prompt-reading chunks run it
+ * (engine.py:283-288). Arguments as dm3_fp8_gemv, plus:
+ *   M          1 <= M <= 2^20; K % 128 == 0, K <= 65536
+ *   workspace  dm3_fp8_gemm_workspace_bytes(M, K) bytes, 256-byte aligned, zero-filled once before
+ *              its first use (only its status word must start at zero; dm3_moe_status reads it);
+ *              calls on one stream may share it
+ */
+int dm3_fp8_gemm(const void* x, int M, int K, int N, const void* q, int64_t ldq, const float* s, int64_t lds,
+                 int srows, const void* bias, int bias_kind, void* y, int64_t ldy, int y_fp32, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 /*
  * Workspace bytes needed by dm3_moe_forward / dm3_moe_layer for hidden H and expert intermediate
  * I (sized for the maximum of 4 rows, so T is ignored). The workspace must be zero-filled once
@@ -145,12 +163,12 @@ int dm3_moe_status(void* workspace, uint32_t* status, void* stream);
  * code running inside another runtime's memory pool, plugin hosts that only hand out their own
  * buffers, or paths where cudaMalloc is not allowed. It has no counterpart in the reference.
  * Arguments and results are those of dm3_moe_layer. The scratch is a 1.5 MiB array compiled
- * into the library, held by every GPU that loads it until the process exits; H <= 2048 and
- * I <= 512 always fit, and sizes beyond the array are rejected with DM3_ENOSPACE. The first
- * call on a device looks up the array's address and zeroes it on the given stream, so make
- * that first call before any stream capture. All calls share the one array and each call leaves
- * it ready for the next, so calls that overlap on the GPU race; the device status word of this
- * scratch is not reported. Allocates nothing.
+ * into the library, held by every GPU that loads it until the process exits; it holds the layer
+ * of H <= 2048 and I <= 512, and larger H or I is rejected with DM3_ENOSPACE. The first call on a
+ * device looks up the array's address and zeroes it, waiting for the clear before it returns, so
+ * make that first call before any stream capture. All calls share the one array and each call
+ * leaves it ready for the next, so calls that overlap on the GPU race. After a device-side
+ * failure read dm3_moe_noalloc_status, which also clears the array. Allocates nothing.
  */
 int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const void* router_w, int router_dtype, int n_router,
                           int top_k, int logits_bf16, const float* logit_bias, const void* w13, int64_t w13_stride,
@@ -158,6 +176,23 @@ int dm3_moe_layer_noalloc(const void* x, int T, int H, int I, const void* router
                           int64_t s2_stride, int srows, const void* sh_w13, const float* sh_s13, const void* sh_w2,
                           const float* sh_s2, int sh_srows, const void* sh_gate, const float* out_bias, void* y,
                           int64_t* ids_out, void* w_out, void* stream);
+
+/*
+ * The status word of the allocation-free layer's static scratch on the current device, as
+ * dm3_moe_status reports it for a workspace (synchronises the stream). A call that stopped at a
+ * bounded wait may leave counters and partial sums in the scratch, so when the word is non-zero
+ * the whole array is zeroed before this returns; the next dm3_moe_layer_noalloc is then correct
+ * again. It has no counterpart in the reference.
+ */
+int dm3_moe_noalloc_status(uint32_t* status, void* stream);
+
+/*
+ * Time limit of every bounded device-side wait (spins on flags, counters and mbarriers) on the
+ * current device, in nanoseconds; 1 s by default. A wait that runs out sets STATUS_TIMEOUT in the
+ * status word and the kernel stops its work uniformly. Call while no kernel of this library runs
+ * on the device. The reference has no device-side waits; this exists for failure detection.
+ */
+int dm3_set_wait_limit_ns(uint64_t ns);
 
 /*
  * Workspace bytes of dm3_moe_prefill / dm3_moe_grouped for T tokens, hidden H, intermediate I,

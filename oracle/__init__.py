@@ -20,6 +20,7 @@ from .moe_oracle import (  # noqa: F401
     dequant,
     fp8_block,
     gemv,
+    linear_dequant,
     moe_forward,
     moe_layer,
     permutation,

@@ -70,6 +70,18 @@ def gemv(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, srows: int = 1, bias
     return out.to(out_dtype)
 
 
+def linear_dequant(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, srows: int = 1, bias=None):
+    """FP8Linear.forward for more than 2 rows (fp8_linear.py:60-63): the weight dequantised
+    (float(q) * scale), cast to x's dtype (bf16), then F.linear in bf16 (products summed exactly
+    here, rounded once to bf16), + bias in bf16."""
+    w = torch.from_numpy(dequant(q, s, srows)).float().to(BF16).double().numpy()
+    y = x.float().numpy().astype(np.float64) @ w.T
+    out = torch.from_numpy(y).float().to(BF16)
+    if bias is not None:
+        out = out + bias.to(BF16)
+    return out
+
+
 # ----------------------------------------------------------------------------- routing
 def router_logits(x: torch.Tensor, gate: torch.Tensor, logits_bf16: bool, logit_bias=None) -> torch.Tensor:
     """fp32 logits x.float() @ gate.T (engine.py:233; exp3_distill.py:36), taken exactly (float64)
