@@ -199,6 +199,74 @@ def time_cpu_port(layers_cpu, budget_s: float):
     return reps / el, reps, torch.get_num_threads()
 
 
+def all_ranks_true(flag: bool, world: int) -> bool:
+    """True when `flag` holds on every rank (every rank takes this collective at the same point)."""
+    if world == 1:
+        return flag
+    import torch.distributed as dist
+
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def check_decode_sharded(grp, world, rank, dev) -> dict:
+    """The sharded decode layer against the one-GPU layer on this rank's GPU, same seeded full layer
+    on every rank: ids and routing weights identical, outputs within 1e-3 relative L2 (the partial
+    sums meet in another order), status word clear."""
+    import drama3_b200 as dm3
+
+    L = make_layer(4321, dev)  # identical on every rank (same seed, same generator)
+    ref = layer_call(L, L["x"])
+    el = E // world
+    sl = slice(rank * el, (rank + 1) * el)
+    errs, ok = [], True
+    for _ in range(2):  # twice: the per-call epoch advances
+        y, ids, w = grp.moe_layer(L["x"], L["gate"], TOPK, True, None, L["w13"][sl], L["s13"][sl], L["w2"][sl],
+                                  L["s2"][sl], L["sh_w13"], L["sh_s13"], L["sh_w2"], L["sh_s2"], L["sh_gate"], None)
+        torch.cuda.synchronize()
+        err = float((y.float() - ref[0].float()).norm() / ref[0].float().norm())
+        errs.append(err)
+        ok = ok and torch.equal(ids, ref[1]) and torch.equal(w, ref[2]) and err < 1e-3
+    ok = ok and dm3.ops.moe_status(dm3.ops.moe_workspace(dev, H, I)) == 0
+    del L
+    ok = all_ranks_true(ok, world)
+    return {"ok": ok, "against": "dm3::moe_layer of the full layer on this rank's GPU (ids, weights equal; y rel-L2)",
+            "rel_l2": [round(e, 7) for e in errs]}
+
+
+def check_prefill_ep(grp, world, rank, dev, placement) -> dict:
+    """The expert-parallel prefill against the one-GPU prefill of all 512 tokens on this rank's GPU,
+    the same seeded full layer on every rank: this rank's outputs, ids and weights bit-identical,
+    status word clear."""
+    import drama3_b200 as dm3
+
+    L = make_prefill_layer(4322, dev)
+    ref = prefill_call(L, L["x"])
+    tl = PF_T // world
+    owner = None
+    if placement == "balanced":
+        owner = dm3.ep.balanced_placement(torch.exp(L["logit_bias"].float().cpu()), world)
+        mine = dm3.ep.local_experts(owner, rank).to(dev)
+        owner = owner.to(dev)
+    else:
+        mine = torch.arange(rank * (E // world), (rank + 1) * (E // world), device=dev)
+    lw = (L["w13"][mine], L["s13"][mine], L["w2"][mine], L["s2"][mine])
+    sl = slice(rank * tl, (rank + 1) * tl)
+    xs = L["x"][sl].contiguous()
+    ok = True
+    for _ in range(2):
+        y, ids, w = grp.moe_prefill(xs, L["gate"], TOPK, True, L["logit_bias"], *lw, L["sh_w13"], L["sh_s13"],
+                                    L["sh_w2"], L["sh_s2"], L["sh_gate"], None, owner=owner)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(y, ref[0][sl]) and torch.equal(ids, ref[1][sl]) and torch.equal(w, ref[2][sl])
+    ok = ok and dm3.ops.moe_status(dm3.ep._ep_workspaces[dev.index]) == 0
+    del L, lw
+    ok = all_ranks_true(ok, world)
+    return {"ok": ok, "against": "dm3::moe_prefill of all 512 tokens with all 256 experts on this rank's GPU "
+                                 "(y, ids, weights bit-identical)"}
+
+
 def run_decode_sharded(args, world, rank, local):
     """One 2-row frame of 40 layers sharded over `world` GPUs: every rank the same rows, router and
     routing, its 256 / world experts per layer (rank 0 the shared expert), and an NVLink all-reduce
@@ -223,6 +291,7 @@ def run_decode_sharded(args, world, rank, local):
         L["w2"], L["s2"] = dm3.fp8_block(torch.randn(el, H, I, generator=gl, device=dev) * 0.02)
         layers.append(L)
     grp = dm3.ep.ExpertParallel(PF_T // world, H, TOPK)
+    parity = check_decode_sharded(grp, world, rank, dev)
 
     def call(L, x):
         return grp.moe_layer(x, L["gate"], TOPK, True, None, L["w13"], L["s13"], L["w2"], L["s2"], L["sh_w13"],
@@ -292,6 +361,7 @@ def run_decode_sharded(args, world, rank, local):
     del graph, g2
     grp.close()
     return {
+        "parity": parity,
         "metric": METRIC, "value": round(n_layers * 1000.0 / ms, 1), "unit": "layer-frames/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "us_per_layer": round(ms * 1000.0 / n_layers, 3), "higher_is_better": True, "scaling": "strong",
@@ -499,6 +569,7 @@ def run_prefill_ep(args, world, rank, local):
         L["x"] = x[rank * tl:(rank + 1) * tl].contiguous()
         layers.append(L)
     grp = dm3.ep.ExpertParallel(tl, H, TOPK)
+    parity = check_prefill_ep(grp, world, rank, dev, placement)
 
     def call(L, x):
         return grp.moe_prefill(x, L["gate"], TOPK, True, L["logit_bias"], L["w13"], L["s13"], L["w2"], L["s2"],
@@ -576,6 +647,7 @@ def run_prefill_ep(args, world, rank, local):
     del graph, g2
     grp.close()
     return {
+        "parity": parity,
         "metric": PF_METRIC,
         "value": round(PF_T * 1000.0 / ms, 1),
         "unit": "tokens/s",
@@ -833,6 +905,126 @@ def run_gemv(args, world, rank, local):
             "shapes": res, "gpu_launches": args.steps * copies * 11}
 
 
+def run_gemm(args, world, rank, local):
+    """Block-FP8 GEMM (dm3::fp8_gemm) for a prompt chunk: M = 256 rows against the 9216 x 2048
+    projection (1x128 scales, the FP8Linear layout), 40 distinct weight copies per graph, next to the
+    reference's own path for more than 2 rows, dequantise + bf16 cast + F.linear (fp8_linear.py:60-61),
+    run with torch on the same GPU and inputs."""
+    import drama3_b200 as dm3
+
+    dev = torch.device("cuda", local)
+    hbm = peaks()["hbm_gbs"]
+    M, N, K, copies = 256, 9216, 2048, 40
+    g = torch.Generator(device=dev).manual_seed(9216)
+    ws = [dm3.quantize(torch.randn(N, K, generator=g, device=dev) * 0.02) for _ in range(copies)]
+    x = rms(torch.randn(M, K, generator=g, device=dev)).to(torch.bfloat16)
+
+    def ours():
+        return [dm3.ops.fp8_gemm(x, q, sc) for q, sc in ws]
+
+    def reference_path():
+        return [torch.nn.functional.linear(x, dm3.dequantize(q, sc).to(x.dtype)) for q, sc in ws]
+
+    res = {}
+    for name, fn in (("ours", ours), ("reference_torch_path", reference_path)):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = fn()
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(args.steps // 5, 4)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (steps * copies)
+        res[name] = {"us": round(us, 2), "outs": outs}
+        del graph
+    err = float((res["ours"]["outs"][0].float() - res["reference_torch_path"]["outs"][0].float()).norm()
+                / res["reference_torch_path"]["outs"][0].float().norm())
+    nbytes = N * K + N * (K // 128) * 4 + M * K * 2 + M * N * 2
+    flops = 2.0 * M * N * K
+    us = res["ours"]["us"]
+    return {"workload": "gemm_fp8_m256_9216x2048_1x128", "rows": M, "K": K, "N": N, "copies": copies,
+            "us": us, "reference_torch_path_us": res["reference_torch_path"]["us"],
+            "speedup_vs_reference_torch_path": round(res["reference_torch_path"]["us"] / us, 2),
+            "rel_l2_vs_reference_torch_path": round(err, 6),
+            "TFLOPs": round(flops / (us * 1e-6) / 1e12, 1),
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / (us * 1e-6) / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4),
+                         "bytes_per_launch": nbytes,
+                         "note": "weights + scales + x + y once; the hi/lo activation split doubles the MMA work"}}
+
+
+def run_audio_head(args, world, rank, local):
+    """The audio head of one CFG frame: the fused block-FP8 head (GEMV, guidance, index_copy into the
+    -inf vocabulary buffer, log-sum-exp) plus direction_score, over 40 distinct head copies per graph,
+    next to the reference's own lines run with torch on the same GPU: the bf16 head matmul, .float(),
+    index_copy into a new -inf buffer and direction_score's log_softmax (engine.py:423-424, :476-479)."""
+    import drama3_b200 as dm3
+
+    dev = torch.device("cuda", local)
+    hbm = peaks()["hbm_gbs"]
+    V, K, NH, copies = 252000, 2048, 4097, 40
+    g = torch.Generator(device=dev).manual_seed(4097)
+    cand = torch.cat([torch.tensor([V - 1], device=dev), torch.arange(151000, 151000 + NH - 1, device=dev)])
+    heads_bf16 = [(torch.randn(NH, K, generator=g, device=dev) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+    ours = [dm3.AudioHead(None, cand, V, *dm3.quantize(w)) for w in heads_bf16]
+    hidden = rms(torch.randn(2, K, generator=g, device=dev)).to(torch.bfloat16)
+    strength = torch.tensor([1.5], dtype=torch.float32, device=dev)
+    token = torch.tensor([151000 + 7], dtype=torch.int64, device=dev)
+    score = torch.zeros((), dtype=torch.float32, device=dev)
+    ref_buf = torch.full((1, V), -torch.inf, device=dev)
+
+    def fused():
+        for h in ours:
+            h(hidden, strength)
+            h.score_into(score, token, V - 1, 151000)
+
+    def reference_path():
+        for w in heads_bf16:
+            logits = (hidden @ w.T).float()
+            ref_buf.index_copy(1, cand, logits[1:] + strength * (logits[:1] - logits[1:]))
+            index = torch.where(token == V - 1, 0, token - 151000 + 1)
+            picked = torch.log_softmax(logits.float(), dim=-1).index_select(1, index.view(1))
+            score.add_((picked[0] - picked[1]).squeeze())
+
+    res = {}
+    for name, fn in (("fused", fused), ("reference_torch_path", reference_path)):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        steps = max(args.steps // 5, 4)
+        e0.record()
+        for _ in range(steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) * 1000.0 / (steps * copies)
+        del graph
+    nbytes = NH * K + NH * (K // 128) * 4 + 2 * K * 2 + 2 * NH * 4 * 2 + NH * 8 + NH * 4
+    us = res["fused"]
+    return {"workload": "audio_head_cfg_4097x2048_fp8_1x128", "candidates": NH, "vocab": V, "copies": copies,
+            "us_per_frame": round(us, 3), "launches_per_frame": 3,
+            "reference_torch_path_us": round(res["reference_torch_path"], 3),
+            "reference_torch_path": "bf16 head matmul + guidance + index_copy into a new -inf buffer + "
+                                    "log_softmax direction_score (torch on the same GPU)",
+            "speedup_vs_reference_torch_path": round(res["reference_torch_path"] / us, 2),
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / (us * 1e-6) / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(nbytes / (us * 1e-6) / 1e9 / hbm, 4), "bytes_per_launch": nbytes}}
+
+
 def run_reference_prefill(args, world):
     """The reference's CPU path for the T=512 prefill layer (torch fp32 on host cores), same metric:
     each step evaluates the whole layer once."""
@@ -905,12 +1097,15 @@ def main():
     ap.add_argument("--layers", type=int, default=40)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="default workload: skip the prefill / GEMV objects (N=1) or the NVLink objects (N>1)")
     ap.add_argument("--decode-mode", default="replicas", choices=["replicas", "sharded"],
                     help="n_gpus > 1 decode: independent replicas (weak scaling) or one frame sharded (strong)")
     ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
                     help="expert placement of the expert-parallel prefill (n_gpus > 1)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
+    parity_ok = True
     try:
         if args.impl == "reference":
             line = run_reference(args, world, rank)
@@ -920,6 +1115,23 @@ def main():
             line = run_prefill(args, world, rank, local)
         else:
             line = run_decode(args, world, rank, local, speaker=args.workload == "speaker")
+            if args.workload == "decode" and not args.decode_only:
+                torch.cuda.empty_cache()
+                if world == 1:
+                    # the prompt-reading layer and the GEMV / GEMM sweep on the same GPU
+                    line["prefill"] = run_prefill(args, world, rank, local)
+                    torch.cuda.empty_cache()
+                    line["gemv"] = run_gemv(args, world, rank, local)
+                    torch.cuda.empty_cache()
+                    line["gemv"]["gemm"] = run_gemm(args, world, rank, local)
+                    torch.cuda.empty_cache()
+                    line["gemv"]["audio_head"] = run_audio_head(args, world, rank, local)
+                else:
+                    # the NVLink paths, each checked against the one-GPU op first
+                    line["prefill_ep"] = run_prefill_ep(args, world, rank, local)
+                    torch.cuda.empty_cache()
+                    line["decode_sharded"] = run_decode_sharded(args, world, rank, local)
+                    parity_ok = line["prefill_ep"]["parity"]["ok"] and line["decode_sharded"]["parity"]["ok"]
         if rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:
@@ -927,6 +1139,8 @@ def main():
             import torch.distributed as dist
 
             dist.destroy_process_group()
+    if not parity_ok:
+        sys.exit("parity check of a multi-GPU path failed")
 
 
 if __name__ == "__main__":

@@ -8,6 +8,7 @@ table read from the checkpoint (`ExpertTable`) and the speaker file reader. Impo
 """
 
 from . import _lib, ep, ops  # noqa: F401
+from .audio_head import AudioHead  # noqa: F401
 from .fp8_linear import BLOCK, FP8Linear, convert, dequantize, quantize  # noqa: F401
 from .fp8_moe import fp8_moe_forward  # noqa: F401
 from .experts import ExpertTable, ResidentExperts, attach_expert_table, read_expert_checkpoint  # noqa: F401

@@ -10,7 +10,7 @@ from pathlib import Path
 PKG_DIR = Path(__file__).resolve().parent
 ROOT = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
-SOURCES = ["abi.cu", "gemm.cu", "gemv.cu", "gemv_tc.cu", "moe_decode.cu", "moe_prefill.cu"]
+SOURCES = ["abi.cu", "gemm.cu", "gemv.cu", "gemv_tc.cu", "head.cu", "moe_decode.cu", "moe_prefill.cu"]
 OUT = PKG_DIR / "libdm3.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -26,6 +26,9 @@ SIGNATURES = {
     "dm3_version": (ctypes.c_char_p, []),
     "dm3_fp8_gemv": (_i, [_p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p, _i, _p, _i64, _i, _p]),
     "dm3_fp8_gemv_gather": (_i, [_p, _i, _i, _i, _p, _i64, _i64, _p, _p, _i64, _i, _p, _i64, _i, _p]),
+    "dm3_audio_head_workspace_bytes": (_sz, [_i]),
+    "dm3_audio_head": (_i, [_p, _i, _p, _i64, _p, _i64, _i, _p, _i64, _i, _p, _p, _p, _i64, _p, _p, _i, _p, _sz, _p]),
+    "dm3_direction_score": (_i, [_p, _p, _i, _p, _i64, _i64, _p, _p]),
     "dm3_fp8_gemm_workspace_bytes": (_sz, [_i, _i]),
     "dm3_fp8_gemm": (_i, [_p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p, _i, _p, _i64, _i, _p, _sz, _p]),
     "dm3_moe_workspace_bytes": (_sz, [_i, _i, _i]),

@@ -5,16 +5,17 @@
 //
 // Two kernels chained by programmatic dependent launch:
 //   split  one warp per token row: the row's absolute maximum gives a power-of-two prescale 2^e
-//          (amax -> [128, 256)); x * 2^e is split exactly into e4m3 hi + lo, stored as rows 2t
-//          (hi) and 2t + 1 (lo) of the activation image, and 2^-e is kept per token
+//          (amax -> [128, 256)); x * 2^e is split exactly into e4m3 hi + lo, stored as row t of the
+//          hi plane and of the lo plane of the activation image, and 2^-e is kept per token
 //   gemm   persistent CTAs over tiles of 128 weight rows x tb tokens (tb = 16, 32, 64 or 128):
 //          warp 0 lane 0 feeds a ring of 4 stages by TMA (the weight slab, 128 rows x 128 bytes of K,
-//          and the activation slab, 2 tb rows, 128-byte swizzle; weights of the first stages go out
-//          before griddepcontrol.wait); warp 1 lane 0 issues tcgen05.mma kind::f8f6f4 (M = 128,
-//          N = 2 tb, K = 32) with one accumulator per 128-wide k block, double-buffered in TMEM;
-//          warps 2-9 (two groups of four, each owning half of the tile's tokens) read every k block's
-//          accumulator, add its hi and lo columns and accumulate them times the weight's block scale
-//          in fp32 registers, then write y = acc * 2^-e (+ bias).
+//          and the tile's hi and lo activation slabs, tb rows each, 128-byte swizzle; weights of the
+//          first stages go out before griddepcontrol.wait); warp 1 lane 0 issues tcgen05.mma
+//          kind::f8f6f4 (M = 128, N = tb, K = 32), the hi and the lo slab into the same accumulator,
+//          one accumulator per 128-wide k block, four of them in flight in TMEM; warps 2-9 (two groups
+//          of four, each owning half of the tile's tokens) read every k block's accumulator with all
+//          loads issued before one wait and accumulate it times the weight's block scale in fp32
+//          registers, then write y = acc * 2^-e (+ bias).
 // Every product is exact (e4m3 x e4m3) and the block scale multiplies each 128-wide k-block partial
 // in fp32, as the reference's dequantise-then-multiply does up to summation order.
 #include <cstdint>
@@ -28,12 +29,13 @@ namespace dm3 {
 namespace gemm {
 
 constexpr int kRows = 128;                       // weight rows per tile (the MMA's M)
-constexpr int kMaxTok = 128;                     // tokens per tile at most (N = 2 tb <= 256)
+constexpr int kMaxTok = 128;                     // tokens per tile at most (the MMA's N)
 constexpr int kStages = 4;
 constexpr int kASlab = kRows * 128;              // 16 KB
-constexpr int kStage = kASlab + 2 * kMaxTok * 128;  // + up to 32 KB of activation rows
-constexpr int kNacc = 2;
-constexpr uint32_t kAccCols = 256;
+constexpr int kBSlab = kMaxTok * 128;            // one activation plane's slab, up to 16 KB
+constexpr int kStage = kASlab + 2 * kBSlab;       // weights, hi rows, lo rows
+constexpr int kNacc = 4;
+constexpr uint32_t kAccCols = 128;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;   // producer, MMA issuer, 8 epilogue warps
 constexpr int kSplitWarps = 8;
@@ -50,7 +52,7 @@ struct Params {
   void* y;
   int64_t ldy;
   int y_fp32;
-  uint8_t* ximg;     // [2 M][K] e4m3
+  uint8_t* ximg;     // [2][M][K] e4m3: the hi plane, then the lo plane
   float* xinv;       // [M]
   uint32_t* ctrl;    // control words; ctrl[kStatusWord] is the sticky status word
   int tb;            // tokens per tile
@@ -65,7 +67,7 @@ __host__ __device__ inline Layout layout(int M, int K) {
   Layout L;
   L.ctrl = 0;
   L.xinv = 256;
-  L.ximg = (L.xinv + static_cast<size_t>(M) * 4 + 1023) / 1024 * 1024;
+  L.ximg = (L.xinv + static_cast<size_t>(M) * 4 + 1023) / 1024 * 1024;  // [2][M][K]
   L.total = L.ximg + static_cast<size_t>(2) * M * K;
   return L;
 }
@@ -104,7 +106,7 @@ __device__ __forceinline__ void split16(const uint4 (&v)[2], float sc, uint4& hi
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// One warp per token row: absolute maximum, then the exact hi / lo split into rows 2t and 2t + 1.
+// One warp per token row: absolute maximum, then the exact hi / lo split into row t of each plane.
 __global__ void __launch_bounds__(32 * kSplitWarps) split_kernel(const __grid_constant__ Params p) {
   const int t = blockIdx.x * kSplitWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   griddep_wait();
@@ -123,8 +125,8 @@ __global__ void __launch_bounds__(32 * kSplitWarps) split_kernel(const __grid_co
   m = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
   const int ex = split_exponent(m);
   const float sc = exp2i(ex);
-  uint8_t* hi_row = p.ximg + static_cast<size_t>(2 * t) * p.K;
-  uint8_t* lo_row = hi_row + p.K;
+  uint8_t* hi_row = p.ximg + static_cast<size_t>(t) * p.K;
+  uint8_t* lo_row = hi_row + static_cast<size_t>(p.M) * p.K;
   for (int c = lane; c < chunks; c += 32) {
     const uint4 v[2] = {__ldg(row + 2 * c), __ldg(row + 2 * c + 1)};
     uint4 hi, lo;
@@ -172,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================================================================ TMA producer (lane 0)
     if (lane == 0) {
       const int total = my_tiles * nkb;
-      const uint32_t bbytes = static_cast<uint32_t>(2 * tb * 128);
+      const uint32_t bbytes = static_cast<uint32_t>(2 * tb * 128);  // hi and lo slabs
       auto tile_of = [&](int k, int& rt, int& tt) {
         const int i = blockIdx.x + k * gridDim.x;
         rt = i / p.n_tok_tiles;
@@ -188,8 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_b = [&](int s) {
         int rt, tt;
         tile_of(s / nkb, rt, tt);
-        tc::tma_load_3d(smem + (s % kStages) * kStage + kASlab, &map_x, (s % nkb) * 128, 2 * tb * tt, 0,
-                        &aux.full[s % kStages]);
+        uint8_t* dst = smem + (s % kStages) * kStage + kASlab;
+        tc::tma_load_3d(dst, &map_x, (s % nkb) * 128, tb * tt, 0, &aux.full[s % kStages]);
+        tc::tma_load_3d(dst + kBSlab, &map_x, (s % nkb) * 128, tb * tt, 1, &aux.full[s % kStages]);
       };
       // weights never come from the preceding kernel: the first ring goes out before the wait
       const int first = min(total, kStages);
@@ -211,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ================================================================ MMA issuer (lane 0)
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_e4m3(kRows, 2 * tb);
+      const uint32_t idesc = tc::idesc_e4m3(kRows, tb);
       const int total = my_tiles * nkb;
       for (int s = 0; s < total; ++s) {
         const int ab = s % kNacc;
@@ -220,9 +223,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         const uint32_t a = smem_u32(smem + (s % kStages) * kStage);
         const uint32_t b = a + kASlab;
+        // x = hi + lo exactly: both halves accumulate into the same columns
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4)
+        for (int k4 = 0; k4 < 4; ++k4) {
           tc::mma_f8(tmem + ab * kAccCols, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+          tc::mma_f8(tmem + ab * kAccCols, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + kBSlab + 32 * k4), idesc,
+                     true);
+        }
         tc::mma_commit(&aux.empty[s % kStages]);
         tc::mma_commit(&aux.acc_full[ab]);
       }
@@ -236,8 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int grp = (warp - 2) >> 2;         // token half of the tile
     const int q = warp & 3;                  // TMEM lane quarter this warp may read
     const int r = 32 * q + lane;             // weight row within the tile
-    const int half = tb / 2;                 // tokens of this group
-    const int nch = half / 8;                // 16-column chunks (8 tokens each) of this group
+    const int half = tb / 2;                 // tokens (= accumulator columns) of this group
     griddep_wait();                          // 2^-e of the tokens comes from the split kernel
     int use = 0;
     for (int k = 0; k < my_tiles; ++k) {
@@ -260,17 +266,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = ok && ready;
         tc::fence_after_sync();
         if (ok) {
-          const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + grp * tb;
-#pragma unroll
-          for (int c = 0; c < kMaxTok / 16; ++c) {
-            if (c < nch) {
-              float v[16];
-              tc::tmem_ld16(ta + 16 * c, v);
-              tc::tmem_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 8; ++j) acc[8 * c + j] = fmaf(sc, v[2 * j] + v[2 * j + 1], acc[8 * c + j]);
-            }
+          const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + grp * half;
+          // every load of this k block is issued before the one wait
+          float v[kMaxTok / 2];
+          if (half == 64) {
+            tc::tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+            tc::tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
+          } else if (half == 32) {
+            tc::tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(&v[0]));
+          } else if (half == 16) {
+            tc::tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(&v[0]));
+          } else {
+            tc::tmem_ld8(ta, *reinterpret_cast<float(*)[8]>(&v[0]));
           }
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < kMaxTok / 2; ++j)
+            if (j < half) acc[j] = fmaf(sc, v[j], acc[j]);
           tc::fence_before_sync();
           __syncwarp();
           if (lane == 0) mbar_arrive(&aux.acc_empty[ab]);
@@ -367,8 +379,8 @@ extern "C" int dm3_fp8_gemm(const void* x, int M, int K, int N, const void* q, i
   CUtensorMap mw, mx;
   if (!dm3::tensor_map_3d(&mw, q, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 1, static_cast<uint64_t>(ldq),
                           static_cast<uint64_t>(ldq) * static_cast<uint64_t>(N), g::kRows) ||
-      !dm3::tensor_map_3d(&mx, p.ximg, static_cast<uint64_t>(K), 2ull * M, 1, static_cast<uint64_t>(K),
-                          2ull * M * static_cast<uint64_t>(K), static_cast<uint32_t>(2 * p.tb)))
+      !dm3::tensor_map_3d(&mx, p.ximg, static_cast<uint64_t>(K), static_cast<uint64_t>(M), 2, static_cast<uint64_t>(K),
+                          static_cast<uint64_t>(M) * static_cast<uint64_t>(K), static_cast<uint32_t>(p.tb)))
     return 2;
   static bool configured[64] = {false};
   if (dev < 64 && !configured[dev]) {

@@ -425,3 +425,84 @@ def noalloc_status() -> int:
     if rc not in (_lib.DM3_OK, _lib.DM3_ETIMEOUT):
         _lib.check(rc, "dm3_moe_noalloc_status")
     return int(st.value)
+
+
+# ----------------------------------------------------------------------------- audio head
+_head_workspaces: dict = {}
+
+
+def _head_workspace(device: torch.device, nbytes: int) -> Tensor:
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _head_workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("drama3_b200: run the audio head once before CUDA-graph capture")
+        ws = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=dev)
+        _head_workspaces[key] = ws
+    return ws
+
+
+@torch.library.custom_op("dm3::audio_head", mutates_args=("vocab",))
+def audio_head(hidden: Tensor, q: Tensor, s: Tensor, strength: Tensor, candidates: Tensor, vocab: Tensor,
+               rows: Optional[Tensor] = None, round_bf16: bool = True) -> tuple[Tensor, Tensor]:
+    """The CFG audio head of one frame (engine.py:423-424): logits = (hidden @ head.T).float() with the
+    block-FP8 head (rows `rows` of q when given, else q itself), then vocab[candidates] = l1 + strength *
+    (l0 - l1) in place (the -inf buffer of CfgGraphs), and each row's log-sum-exp for direction_score.
+    hidden bf16 [2, K]; strength fp32 device scalar; candidates int64 [Nc]. Returns (logits fp32 [2, Nc],
+    lse fp32 [2])."""
+    _require_cuda(hidden, q, s, strength, candidates, vocab, rows)
+    lib = _lib.load()
+    q = _fp8_bytes(q)
+    hidden = hidden.to(BF16).contiguous()
+    if hidden.dim() != 2 or hidden.shape[0] != 2:
+        raise RuntimeError("the audio head takes the 2 guidance rows [2, K]")
+    K = hidden.shape[1]
+    Nc = candidates.numel()
+    if q.stride(1) != 1 or q.shape[1] != K:
+        raise RuntimeError("q must be [rows, K] with unit column stride")
+    if vocab.dtype != torch.float32 or not vocab.is_contiguous():
+        raise RuntimeError("vocab must be a contiguous fp32 buffer")
+    if strength.dtype != torch.float32 or strength.numel() != 1:
+        raise RuntimeError("strength must be a one-element fp32 device tensor")
+    candidates = candidates.to(torch.int64).contiguous()
+    if rows is not None:
+        rows = rows.to(torch.int64).contiguous()
+        if rows.numel() != Nc:
+            raise RuntimeError("rows and candidates must have the same length")
+    else:
+        if q.shape[0] != Nc:
+            raise RuntimeError("without rows, q must hold exactly the candidate rows")
+    srows = scale_rows(q.shape[0], s.shape[0])
+    s = s.contiguous()
+    logits = torch.empty((2, Nc), dtype=torch.float32, device=hidden.device)
+    lse = torch.empty((2,), dtype=torch.float32, device=hidden.device)
+    ws = _head_workspace(hidden.device, lib.dm3_audio_head_workspace_bytes(Nc))
+    rc = lib.dm3_audio_head(_ptr(hidden), K, _ptr(q), q.stride(0), _ptr(s), s.stride(0), srows, _ptr(rows), q.shape[0],
+                            Nc, _ptr(strength), _ptr(candidates), _ptr(vocab), vocab.numel(), _ptr(logits), _ptr(lse),
+                            1 if round_bf16 else 0, _ptr(ws), ws.numel(), _stream(hidden.device))
+    _lib.check(rc, "dm3_audio_head")
+    return logits, lse
+
+
+@audio_head.register_fake
+def _(hidden, q, s, strength, candidates, vocab, rows=None, round_bf16=True):
+    return (hidden.new_empty((2, candidates.numel()), dtype=torch.float32), hidden.new_empty((2,), dtype=torch.float32))
+
+
+@torch.library.custom_op("dm3::direction_score", mutates_args=("score",))
+def direction_score(logits: Tensor, lse: Tensor, token: Tensor, eos_id: int, semantic_begin: int,
+                    score: Tensor) -> None:
+    """score += log_softmax(logits)[0, i] - log_softmax(logits)[1, i] with i = 0 for the eos token and
+    token - semantic_begin + 1 otherwise (engine.py:476-479), all on the device (token int64 scalar)."""
+    _require_cuda(logits, lse, token, score)
+    if score.dtype != torch.float32 or token.dtype != torch.int64:
+        raise RuntimeError("score must be fp32 and token int64")
+    rc = _lib.load().dm3_direction_score(_ptr(logits), _ptr(lse), logits.shape[1], _ptr(token), int(eos_id),
+                                         int(semantic_begin), _ptr(score), _stream(logits.device))
+    _lib.check(rc, "dm3_direction_score")
+
+
+@direction_score.register_fake
+def _(logits, lse, token, eos_id, semantic_begin, score):
+    return None

@@ -73,6 +73,39 @@ int dm3_fp8_gemv_gather(const void* x, int M, int K, int N, const void* q, int64
                         const int64_t* rows, const float* s, int64_t lds, int srows, void* y, int64_t ldy,
                         int y_fp32, void* stream);
 
+/* Workspace bytes of dm3_audio_head for Nc candidate rows. */
+size_t dm3_audio_head_workspace_bytes(int Nc);
+
+/*
+ * The audio head of one CFG decode frame (engine.py:423-424, head of engine.py:409-410): the
+ * block-FP8 GEMV logits[2, Nc] = hidden[2, K] @ head[Nc, K]^T (fp32, rounded to bf16 first when
+ * round_bf16, the dtype the reference's bf16 head or FP8Linear returns), then
+ * vocab[cols[j]] = l1[j] + strength * (l0[j] - l1[j]) with the reference's three fp32 roundings
+ * (index_copy into the -inf buffer; entries outside cols are not touched), and lse[r] =
+ * log-sum-exp of row r for direction_score. Two launches instead of a GEMV and about five
+ * elementwise kernels, no vocabulary-wide allocation.
+ *   x         bf16 [2, K] (row 0 conditional, row 1 unconditional)
+ *   q, s      e4m3 head [Nc, K] (rows == null) or the full matrix [n_rows_q, K] with rows int64 [Nc]
+ *             choosing the candidates; scale layout srows as dm3_fp8_gemv
+ *   strength  device fp32 scalar (CfgGraphs keeps it as a device tensor)
+ *   cols      device int64 [Nc]: vocabulary column of each candidate (the candidates tensor)
+ *   vocab     fp32 [V], filled with -inf once by the caller
+ *   logits    fp32 [2, Nc] out; lse fp32 [2] out
+ *   workspace dm3_audio_head_workspace_bytes(Nc), zero-filled once, 256-byte aligned
+ */
+int dm3_audio_head(const void* x, int K, const void* q, int64_t ldq, const float* s, int64_t lds, int srows,
+                   const int64_t* rows, int64_t n_rows_q, int Nc, const float* strength, const int64_t* cols,
+                   float* vocab, int64_t V, float* logits, float* lse, int round_bf16, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/*
+ * direction_score (engine.py:476-479) accumulated on the device: *score += (logits[0, i] - lse[0])
+ * - (logits[1, i] - lse[1]) with i = 0 when *token == eos_id, else *token - semantic_begin + 1;
+ * logits / lse as dm3_audio_head wrote them, token a device int64 (the sampled frame's first code).
+ */
+int dm3_direction_score(const float* logits, const float* lse, int Nc, const int64_t* token, int64_t eos_id,
+                        int64_t semantic_begin, float* score, void* stream);
+
 /* Workspace bytes of dm3_fp8_gemm for M activation rows of K elements. */
 size_t dm3_fp8_gemm_workspace_bytes(int M, int K);
 

@@ -16,6 +16,8 @@ exp3_distill.py:34-48).
 
 from .moe_oracle import (  # noqa: F401
     BLOCK,
+    audio_head,
+    direction_score,
     FP8_MAX,
     dequant,
     fp8_block,

@@ -227,3 +227,23 @@ def moe_layer(x, gate, experts: dict, top_k=8, logits_bf16=True, logit_bias=None
         sh = shared_expert(x, sw)
         y = (y.float() + (sg.float()[:, None] * sh.float()).to(BF16).float()).to(BF16)
     return y, ids, w
+
+
+# ----------------------------------------------------------------------------- audio head
+def audio_head(hidden, q, s, srows: int, candidates, vocab_size: int, strength: float):
+    """CfgGraphs.run's head lines (engine.py:423-424) with the block-FP8 head: logits = the head GEMV
+    in the activations' dtype (bf16, as the Triton `_gemv` or the bf16 matmul returns), .float();
+    guided = a [1, vocab] -inf buffer with the candidate columns set to l1 + strength * (l0 - l1)
+    (fp32, torch's own ops). Returns (logits fp32 [2, Nc], guided fp32 [1, vocab])."""
+    logits = gemv(hidden, q, s, srows).float()
+    st = torch.tensor(strength, dtype=torch.float32)
+    guided = torch.full((1, vocab_size), -torch.inf).index_copy(1, candidates, logits[1:] + st * (logits[:1] - logits[1:]))
+    return logits, guided
+
+
+def direction_score(logits, token: int, eos_id: int, semantic_begin: int):
+    """engine.direction_score (engine.py:476-479): log-softmax of both rows at the sampled token's
+    column (0 for eos, else token - semantic_begin + 1), conditional minus unconditional."""
+    index = 0 if token == eos_id else token - semantic_begin + 1
+    picked = torch.log_softmax(logits.float(), dim=-1)[:, index]
+    return (picked[0] - picked[1]).reshape(())
