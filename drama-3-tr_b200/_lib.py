@@ -25,6 +25,7 @@ SIGNATURES = {
     "dm3_last_error": (ctypes.c_char_p, []),
     "dm3_version": (ctypes.c_char_p, []),
     "dm3_fp8_gemv": (_i, [_p, _i, _i, _i, _p, _i64, _p, _i64, _i, _p, _i, _p, _i64, _i, _p]),
+    "dm3_gemv_status": (_i, [_u32p, _p]),
     "dm3_fp8_gemv_gather": (_i, [_p, _i, _i, _i, _p, _i64, _i64, _p, _p, _i64, _i, _p, _i64, _i, _p]),
     "dm3_audio_head_workspace_bytes": (_sz, [_i]),
     "dm3_audio_head": (_i, [_p, _i, _p, _i64, _p, _i64, _i, _p, _i64, _i, _p, _p, _p, _i64, _p, _p, _i, _p, _sz, _p]),

@@ -15,10 +15,14 @@
 //             TMEM accumulator of 16 columns per 128-wide k block
 //   warps 4-7 read TMEM (one weight row per thread), apply the fp32 block scales per k block and
 //             the prescale, and leave the chunk's partial sums in shared memory
-// The cluster then sums the partials of each row over its CTAs in a fixed order through
-// distributed shared memory (each CTA finishes 128 / split rows), adds the bias and writes y.
-// Cluster barriers are the only synchronisation between CTAs. The per-block scale multiplies each
+// Each CTA then owns 128 / split rows of the tile: every epilogue thread pushes its row's partial
+// sums (16 bytes) into the owner's shared memory with st.async, counted on the owner's mbarrier;
+// the owner sums the split partials in rank order (a fixed order, so the result does not depend on
+// arrival order), adds the bias and writes y. No cluster-wide barrier sits on the path after the
+// MMAs: one cluster barrier at kernel start (arrive early, wait just before the first push) makes
+// every CTA's mbarrier initialisation visible to the others. The per-block scale multiplies each
 // 128-wide k-block partial in fp32, as the reference Triton kernel does (fp8_linear.py:21-26).
+// A bounded wait that runs out sets a bit in the library's GEMV status word (dm3_gemv_status).
 #include <cooperative_groups.h>
 
 #include "dm3_common.cuh"
@@ -29,6 +33,40 @@ namespace cg = cooperative_groups;
 
 namespace dm3 {
 namespace gemv_tc {
+
+// Split cluster barrier: every thread arrives (release) after initialisation and waits (acquire)
+// once, before it first touches another CTA's shared memory.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_async16(uint32_t raddr, uint4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   raddr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  auto try_once = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_once()) return true;
+  const uint64_t t0 = globaltimer();
+  while (!try_once()) {
+    if (globaltimer() - t0 > wait_limit_ns()) return false;
+  }
+  return true;
+}
 
 constexpr int kThreads = 256;
 constexpr int kTileRows = 128;
@@ -53,15 +91,18 @@ struct Params {
   int y_fp32;
   int split;  // CTAs per cluster (K chunks)
   int nsl;    // slabs per CTA
-  uint32_t* status;  // optional word for bounded-wait timeouts (null: not reported)
 };
 
+// Sticky status of every tensor-core GEMV launch on this device (dm3_gemv_status reads and clears it).
+static __device__ uint32_t g_status;
+
 struct Aux {
-  uint64_t full, done;
+  uint64_t full, done, rx_full;
   uint32_t tmem;
   uint32_t xmax[kMaxT];
   float xinv[kMaxT];
-  float part[kTileRows][kMaxT];  // this chunk's partial sums
+  // partial sums of the rows this CTA owns: [source rank][row within the owned block][token]
+  alignas(16) float recv[kTileRows][kMaxT];
 };
 
 __host__ __device__ inline int smem_bytes(int nsl) {
@@ -96,17 +137,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
   uint8_t* b_tile = smem + nsl * kSlabBytes;
   Aux& aux = *reinterpret_cast<Aux*>(b_tile + nsl * kBSlabBytes);
 
+  const int per = kTileRows / p.split;  // rows owned by each CTA of the cluster
   if (tid == 0) {
     tc::prefetch_map(&map_q);
     mbar_init(&aux.full, 1);
     mbar_init(&aux.done, 1);
+    mbar_init(&aux.rx_full, 1);
     fence_mbar_init();
+    // armed before the cluster barrier's arrival, so no peer's push can come first
+    mbar_arrive_expect_tx(&aux.rx_full, static_cast<uint32_t>((p.split - 1) * per * 16));
   }
   if (tid < kMaxT) aux.xmax[tid] = 0u;
   if (warp == 1) tc::tmem_alloc(&aux.tmem, kTmemCols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
+  cluster_arrive();
   const uint32_t tmem = aux.tmem;
 
   if (warp == 0) {
@@ -165,14 +211,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
       tc::fence_after_sync();
       const uint32_t idesc = tc::idesc_e4m3(kTileRows, kN);
       const uint32_t a = smem_u32(a_tiles), b = smem_u32(b_tile);
-      for (int j = 0; j < nsl; ++j)
+      // k step outer, slab inner: consecutive MMAs go to different accumulators
 #pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4)
+      for (int k4 = 0; k4 < 4; ++k4)
+        for (int j = 0; j < nsl; ++j)
           tc::mma_f8(tmem + j * 16, tc::smem_desc(a + j * kSlabBytes + 32 * k4), tc::smem_desc(b + j * kBSlabBytes + 32 * k4),
                      idesc, k4 > 0);
       tc::mma_commit(&aux.done);
-    } else if (p.status) {
-      atomicOr(p.status, STATUS_TIMEOUT);
+    } else {
+      atomicOr(&g_status, STATUS_TIMEOUT);
     }
   }
   if (warp >= 4) {
@@ -186,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
     bool ready = true;
     if (lane == 0) ready = mbar_wait(&aux.done, 0);
     ready = __shfl_sync(0xffffffffu, ready, 0);
-    if (!ready && lane == 0 && p.status) atomicOr(p.status, STATUS_TIMEOUT);
+    if (!ready && lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
     tc::fence_after_sync();
     float acc[kMaxT] = {0.f, 0.f, 0.f, 0.f};
     float v[kMaxSlabs][8];
@@ -200,23 +247,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
       if (j < nsl)
 #pragma unroll
         for (int t = 0; t < kMaxT; ++t) acc[t] = fmaf(sc[j], v[j][t] + v[j][4 + t], acc[t]);
-#pragma unroll
-    for (int t = 0; t < kMaxT; ++t) aux.part[r][t] = ready ? acc[t] * aux.xinv[t] : 0.f;
+    const float4 v4 = ready ? make_float4(acc[0] * aux.xinv[0], acc[1] * aux.xinv[1], acc[2] * aux.xinv[2],
+                                          acc[3] * aux.xinv[3])
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
     tc::fence_before_sync();
-  }
-  cluster.sync();  // every CTA's partials are in its shared memory
-  // this CTA finishes rows [rank * 128 / split, (rank + 1) * 128 / split) of the tile
-  {
-    const int per = kTileRows / p.split;
-    for (int i = tid; i < per * p.M; i += kThreads) {
-      const int rr = rank * per + i / p.M, t = i % p.M;
-      const int n = tile * kTileRows + rr;
-      if (n < p.N) {
+    // this row's partials to the CTA owning it: slot [my rank][row within the owned block]
+    const int owner = r / per;
+    const uint32_t slot = smem_u32(&aux.recv[rank * per + r % per][0]);
+    cluster_wait();  // every CTA's rx_full is initialised and armed
+    if (owner == rank) {
+      *reinterpret_cast<float4*>(&aux.recv[rank * per + r % per][0]) = v4;
+    } else {
+      const uint4 u = make_uint4(__float_as_uint(v4.x), __float_as_uint(v4.y), __float_as_uint(v4.z),
+                                 __float_as_uint(v4.w));
+      st_async16(mapa_shared(slot, static_cast<uint32_t>(owner)), u,
+                 mapa_shared(smem_u32(&aux.rx_full), static_cast<uint32_t>(owner)));
+    }
+    named_bar(1, 128);  // the owned rows' own partials are in shared memory
+    bool got = true;
+    if (p.split > 1) {
+      if (lane == 0) got = mbar_wait_cluster(&aux.rx_full, 0);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got && lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
+    }
+    // the owned rows [rank * per, (rank + 1) * per): sum over the source ranks in order, + bias
+    const int et = tid - 128;
+    for (int i = et; i < per * p.M; i += 128) {
+      const int t = i / per, rr = i % per;
+      const int n = tile * kTileRows + rank * per + rr;
+      if (n < p.N && got) {
         float sum = 0.f;
-        for (int q = 0; q < p.split; ++q) {
-          const Aux* ra = cluster.map_shared_rank(&aux, q);
-          sum += ra->part[rr][t];
-        }
+        for (int q = 0; q < p.split; ++q) sum += aux.recv[q * per + rr][t];
         if (p.bias_kind == 1) sum += __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
         if (p.bias_kind == 2) sum += static_cast<const float*>(p.bias)[n];
         if (p.y_fp32)
@@ -225,8 +286,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
           static_cast<__nv_bfloat16*>(p.y)[t * p.ldy + n] = __float2bfloat16_rn(sum);
       }
     }
+  } else {
+    __syncwarp();    // warp 1 reconverges after its lane 0 issued the MMAs
+    cluster_wait();  // every thread that arrived waits once
   }
-  cluster.sync();  // no CTA leaves while another still reads its partials
+  tc::fence_before_sync();
+  __syncthreads();
   tc::fence_after_sync();
   if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
 }
@@ -247,11 +312,13 @@ int launch_gemv_tc(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q
     return 2;
   }
   const int sms = sm_count(dev);
-  // largest power-of-two split <= 8 that divides the slabs, keeps <= 8 slabs per CTA and does not
-  // exceed the SM count by more than a few percent
+  // the largest power-of-two split <= 8 that divides the slabs and does not exceed the SM count by
+  // more than a few percent, raised until a CTA holds at most 4 slabs (64 KB): two CTAs then fit an
+  // SM, so a chain's next GEMV loads its weights beside this one (measured on a 40-call chain:
+  // 2048 x 8192 takes 5.6 µs per call at split 4, 6.3 at split 2)
   int split = 1;
   while (split * 2 <= kMaxSplit && slabs % (split * 2) == 0 && tiles * split * 2 <= sms + sms / 16) split *= 2;
-  while (slabs / split > kMaxSlabs && split * 2 <= kMaxSplit && slabs % (split * 2) == 0) split *= 2;
+  while (slabs / split > 4 && split * 2 <= kMaxSplit && slabs % (split * 2) == 0) split *= 2;
   if (slabs / split > kMaxSlabs || slabs % split) return -1;
   Params p{};
   p.x = x;
@@ -268,7 +335,6 @@ int launch_gemv_tc(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q
   p.y_fp32 = y_fp32;
   p.split = split;
   p.nsl = slabs / split;
-  p.status = nullptr;
   CUtensorMap mq;
   if (!tensor_map_3d(&mq, q, static_cast<uint64_t>(K), static_cast<uint64_t>(N), 1, static_cast<uint64_t>(ldq),
                      static_cast<uint64_t>(ldq) * static_cast<uint64_t>(N), kTileRows))
@@ -311,3 +377,16 @@ namespace dm3 {
 // This file's copy of the device wait limit on the current device (dm3_set_wait_limit_ns).
 int wait_limit_gemv_tc(uint64_t ns) { return static_cast<int>(set_wait_limit_here(ns)); }
 }  // namespace dm3
+
+extern "C" int dm3_gemv_status(uint32_t* status, void* stream) {
+  if (!status) return dm3::set_error("null pointer argument"), 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  const uint32_t zero = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, dm3::gemv_tc::g_status, 4, 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaMemcpyToSymbolAsync(dm3::gemv_tc::g_status, &zero, 4, 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return dm3::set_error("reading the GEMV status word failed"), 2;
+  *status = v;
+  return (v & dm3::STATUS_TIMEOUT) ? 3 : 0;
+}

@@ -51,7 +51,6 @@ struct FAux {
   uint64_t dacc_full[kFMaxTiles];     // down blocks: MMAs done
   uint32_t tmem;
   int epi_ok[4];
-  int final_cta;                      // this CTA counted last: it converts the sums
   int n_slots;
   float xinv[kMaxT];
   float upv[kUpHalf][kMaxT];
@@ -61,6 +60,13 @@ struct FAux {
   alignas(16) uint8_t hstage[kHxRows][kUpHalf];   // this CTA's h bytes before they are sent
   Table tab;
   RouteTail rt;
+  // the fast selection (T <= 2): each row's candidates as (logit order, ~expert) keys in ascending
+  // expert order, their count (kMaxCand + 1 = too many), the row's logit maximum and softmax sum
+  uint64_t ckey[2][32];
+  int ncand[2];
+  float rmax[2], rz[2];
+  int sel_e[2][kMaxTopK];
+  float sel_v[2][kMaxTopK];
 };
 
 // Shared memory of the cluster kernel from a 1024-byte aligned base: the ring, the x image (16 rows
@@ -174,6 +180,106 @@ template <int N>
 __device__ __forceinline__ void hold(const float (&v)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) asm volatile("" ::"f"(v[i]));
+}
+
+// Row t's candidates, found by an otherwise idle warp while another takes the row's softmax sum:
+// every expert whose logit is at least theta, the top_k-th largest of the 32 lane maxima (each lane
+// holds 8 logits). The top_k-th largest logit is at least theta, so the set holds every expert the
+// row can select (usually a few more). Their (logit order, ~expert) keys go to shared memory in
+// ascending expert order, with their count. (Asking L2 for the candidates' weights from here was
+// measured and dropped: the bulk prefetches queue in the SM's copy engine ahead of the CTA's own
+// weight copies and made the layer slower.)
+__device__ void find_candidates(const Params& p, const RouteTail& rt, int t, int lane, uint64_t* ckey, int* ncand) {
+  const int E = p.n_router, K = p.top_k;
+  float lv[8];
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    lv[i] = lane + 32 * i < E ? rt.logits[t][lane + 32 * i] : -FLT_MAX;
+    m = fmaxf(m, lv[i]);
+  }
+  // rank of this lane's maximum among the 32 (ties to the lower lane): a permutation of 0..31
+  int beats = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const float o = __shfl_sync(0xffffffffu, m, j);
+    beats += (o > m || (o == m && j < lane)) ? 1 : 0;
+  }
+  const unsigned who = __ballot_sync(0xffffffffu, beats == K - 1);
+  const float theta = __shfl_sync(0xffffffffu, m, __ffs(who) - 1);
+  // candidate index of (lane, i): the candidates of the columns before i, then of the lanes before
+  int base = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool c = lane + 32 * i < E && lv[i] >= theta;
+    const unsigned bal = __ballot_sync(0xffffffffu, c);
+    const int k = base + __popc(bal & ((1u << lane) - 1u));
+    if (c && k < 32)
+      ckey[k] = (static_cast<uint64_t>(order_key(lv[i])) << 32) | static_cast<uint32_t>(~(lane + 32 * i));
+    base += __popc(bal);
+  }
+  if (lane == 0) *ncand = base;
+}
+
+// Row t's logit maximum and softmax denominator, in the order route_row sums them (each lane its 8
+// logits in index order, then the butterfly), so the routing weights come out identical.
+__device__ void row_softmax_sum(const Params& p, const RouteTail& rt, int t, int lane, float& m_out, float& z_out) {
+  const int E = p.n_router;
+  float lv[8];
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    lv[i] = lane + 32 * i < E ? rt.logits[t][lane + 32 * i] : -FLT_MAX;
+    m = fmaxf(m, lv[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float z = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    if (lane + 32 * i < E) z += expf(lv[i] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+  m_out = m;
+  z_out = z;
+}
+
+// The top_k of row t from its candidates (every expert that can be selected, at most 32): lane c
+// ranks candidate c by counting the larger keys, which gives the order of route_row's merge (logit
+// descending, ties to the lower expert); then softmax weights and renormalisation as route_row.
+__device__ void route_row_candidates(const Params& p, FAux& aux, int t, int lane, bool emit) {
+  const int K = p.top_k, nc = aux.ncand[t];
+  const uint64_t mine = lane < nc ? aux.ckey[t][lane] : 0ull;
+  int rank = 0;
+  for (int j = 0; j < nc; ++j) rank += aux.ckey[t][j] > mine ? 1 : 0;
+  if (lane < nc && rank < K) {
+    aux.sel_e[t][rank] = static_cast<int>(~static_cast<uint32_t>(mine));
+    aux.sel_v[t][rank] = key_value(static_cast<uint32_t>(mine >> 32));
+  }
+  __syncwarp();
+  const float m = aux.rmax[t], z = aux.rz[t];
+  int my_e = 0;
+  float my_v = 0.f;
+  if (lane < K) {
+    my_e = aux.sel_e[t][lane];
+    my_v = aux.sel_v[t][lane];
+  }
+  const float my_p = expf(my_v - m) / z;
+  float psum = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxTopK; ++j) {
+    const float pj = __shfl_sync(0xffffffffu, my_p, j);
+    if (j < K) psum += pj;
+  }
+  RouteTail& rt = aux.rt;
+  if (lane < K) {
+    const __nv_bfloat16 wb = __float2bfloat16_rn(my_p / psum);
+    rt.sel_e[t * K + lane] = my_e;
+    rt.sel_w[t * K + lane] = __bfloat162float(wb);
+    if (emit && p.ids_out) p.ids_out[t * K + lane] = my_e;
+    if (emit && p.w_out) p.w_out[t * K + lane] = wb;
+  }
+  if (lane == 0) rt.shared_coef[t] = p.sh_gate ? bf16_round(1.f / (1.f + expf(-rt.logits[t][p.n_router]))) : 1.f;
 }
 
 // The four epilogue warps wait for one mbarrier phase (lane 0 of each, bounded) and continue only
@@ -295,49 +401,50 @@ __device__ __forceinline__ void cl_epilogue_down(const Params& p, const WsLayout
   }
 }
 
-// The sums of output rows [half H/2, half H/2 + H/2) to y, by every thread of the CTA that counted
-// last for that half, with the rounding points of combine_kernel:
+// The fixed-point sums to y, after the cluster kernel has completed: one thread per pair of output
+// elements, with the rounding points of combine_kernel,
 // y = bf16(bf16(bf16(routed) + bias) + bf16(sigmoid gate * bf16(shared))); the sums are cleared for
 // the next call. A sum converts to fp32 with one rounding (int64 -> float, then an exact 2^-36).
-// Four pairs of elements per thread and pass, every load of a pass issued first.
-__device__ void cl_finish(const Params& p, const WsLayout& L, const FAux& aux, int tid, int half) {
-  constexpr int kB = 4;
+// Kernel completion orders every CTA's reductions before these loads, so the cluster kernel needs
+// no fence, counter or last-CTA step of its own; the bias is requested before griddepcontrol.wait.
+constexpr int kFinishThreads = 256;
+__global__ void __launch_bounds__(kFinishThreads) finish_kernel(const __grid_constant__ Params p) {
+  const WsLayout L = ws_layout(p.H, p.I);
+  const int i = (blockIdx.x * kFinishThreads + threadIdx.x) * 2;  // first of two consecutive outputs
+  const bool active = i < p.T * p.H;
+  const int t = active ? i / p.H : 0, n = active ? i % p.H : 0;
+  float b0 = 0.f, b1 = 0.f;
+  if (active && p.out_bias) {
+    b0 = __ldg(p.out_bias + n);
+    b1 = __ldg(p.out_bias + n + 1);
+  }
+  griddep_wait();
+  griddep_launch();
+  if (!active) return;
   long long* fa = reinterpret_cast<long long*>(p.ws + L.facc);
   const size_t shared_off = static_cast<size_t>(kMaxT) * p.H;
-  const int hh = p.H / 2, n_out = p.T * hh;
+  const size_t off = static_cast<size_t>(t) * p.H + n;
+  const longlong2 R = __ldcg(reinterpret_cast<const longlong2*>(fa + off));
   const bool sh = p.sh_w13 != nullptr;
-  const float unit = 1.0f / kFixScale;
-  for (int i0 = 0; i0 < n_out; i0 += kThreads * 2 * kB) {
-    longlong2 R[kB], S[kB];
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      const int i = i0 + (b * kThreads + tid) * 2;
-      if (i < n_out) {
-        const int off = (i / hh) * p.H + half * hh + i % hh;
-        R[b] = __ldcg(reinterpret_cast<const longlong2*>(fa + off));
-        S[b] = __ldcg(reinterpret_cast<const longlong2*>(fa + shared_off + off));
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < kB; ++b) {
-      const int i = i0 + (b * kThreads + tid) * 2;
-      if (i >= n_out) break;
-      const int t = i / hh, n = half * hh + i % hh, off = t * p.H + n;
-      const float g = sh ? aux.rt.shared_coef[t] : 0.f;
-      float y0 = bf16_round(__ll2float_rn(R[b].x) * unit), y1 = bf16_round(__ll2float_rn(R[b].y) * unit);
-      if (p.out_bias) {
-        y0 = bf16_round(y0 + __ldg(p.out_bias + n));
-        y1 = bf16_round(y1 + __ldg(p.out_bias + n + 1));
-      }
-      if (sh) {
-        y0 += bf16_round(g * bf16_round(__ll2float_rn(S[b].x) * unit));
-        y1 += bf16_round(g * bf16_round(__ll2float_rn(S[b].y) * unit));
-      }
-      *reinterpret_cast<__nv_bfloat162*>(p.y + off) = __floats2bfloat162_rn(y0, y1);
-      __stcg(reinterpret_cast<longlong2*>(fa + off), make_longlong2(0, 0));
-      __stcg(reinterpret_cast<longlong2*>(fa + shared_off + off), make_longlong2(0, 0));
-    }
+  longlong2 S = make_longlong2(0, 0);
+  float g = 0.f;
+  if (sh) {
+    S = __ldcg(reinterpret_cast<const longlong2*>(fa + shared_off + off));
+    g = __ldcg(reinterpret_cast<const float*>(p.ws + L.gate) + t);
   }
+  const float unit = 1.0f / kFixScale;
+  float y0 = bf16_round(__ll2float_rn(R.x) * unit), y1 = bf16_round(__ll2float_rn(R.y) * unit);
+  if (p.out_bias) {
+    y0 = bf16_round(y0 + b0);
+    y1 = bf16_round(y1 + b1);
+  }
+  if (sh) {
+    y0 += bf16_round(g * bf16_round(__ll2float_rn(S.x) * unit));
+    y1 += bf16_round(g * bf16_round(__ll2float_rn(S.y) * unit));
+  }
+  *reinterpret_cast<__nv_bfloat162*>(p.y + off) = __floats2bfloat162_rn(y0, y1);
+  __stcg(reinterpret_cast<longlong2*>(fa + off), make_longlong2(0, 0));
+  if (sh) __stcg(reinterpret_cast<longlong2*>(fa + shared_off + off), make_longlong2(0, 0));
 }
 
 // x split into the up MMAs' B operand by the 64 threads of warps 2-3 (which are otherwise idle while
@@ -444,7 +551,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     // armed before the cluster barrier below, so no peer's st.async can reach it earlier
     mbar_arrive_expect_tx(&aux.hx_full, kCl * kHxBytesPerSrc);
-    aux.final_cta = 0;
   }
   if (warp == kWarpMma) tc::tmem_alloc(&aux.tmem, kFTmemCols);
   tc::fence_before_sync();
@@ -589,8 +695,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     named_bar(kBarEpi, kEpiThreads);
-    if (e < p.T) route_row(p, aux.rt, e, lane, blockIdx.x == 0);
+    if (p.T <= 2) {
+      // warps 4..4+T-1 take each row's maximum and softmax sum while warps 4+T.. find the row's
+      // candidates; then the first warps rank the candidates
+      if (e < p.T)
+        row_softmax_sum(p, aux.rt, e, lane, aux.rmax[e], aux.rz[e]);
+      else if (e < 2 * p.T)
+        find_candidates(p, aux.rt, e - p.T, lane, aux.ckey[e - p.T], &aux.ncand[e - p.T]);
+      named_bar(kBarEpi, kEpiThreads);
+      if (e < p.T) {
+        if (aux.ncand[e] <= 32)
+          route_row_candidates(p, aux, e, lane, blockIdx.x == 0);
+        else
+          route_row(p, aux.rt, e, lane, blockIdx.x == 0);  // ties over more than 32 experts
+      }
+    } else if (e < p.T) {
+      route_row(p, aux.rt, e, lane, blockIdx.x == 0);
+    }
     named_bar(kBarEpi, kEpiThreads);
+    if (blockIdx.x == 0 && et < p.T) reinterpret_cast<float*>(p.ws + L.gate)[et] = aux.rt.shared_coef[et];
     if (e == 0) {
       const int n = table_smem(p, aux.rt, lane, aux.tab);
       if (lane == 0) aux.n_slots = n;
@@ -631,22 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         cl_epilogue_down<4>(p, L, aux, tmem + tlane + 256u + 32u * j, slot, shared_slot, row_base + kBlockRows * j + r,
                             &sc2[j], min(4, ntiles - j));
       }
-      if (ok) {
-        // count this CTA's sums; the last CTA of the call converts them (after the barrier below)
-        named_bar(kBarEpi, kEpiThreads);
-        if (et == 0) {
-          __threadfence();  // cumulative over the CTA's reductions, ordered by the barrier above
-          // one count per half of the output rows: the two halves are converted by two CTAs
-          const uint32_t old = atomicAdd(ctrl(p, L) + CTRL_FCOUNT + q, 1u);
-          if (old == static_cast<uint32_t>(aux.n_slots * nq - 1)) {
-            __threadfence();
-            ctrl(p, L)[CTRL_FCOUNT + q] = 0u;  // every CTA of this half has counted: ready for the next call
-            aux.final_cta = 1;
-          }
-        }
-      } else if (et == 0) {
-        flag_error(p, L, STATUS_TIMEOUT);
-      }
+      if (!ok && et == 0) flag_error(p, L, STATUS_TIMEOUT);
+
     }
   }
 
@@ -654,5 +763,4 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == kWarpMma) tc::tmem_dealloc(tmem, kFTmemCols);
-  if (aux.final_cta) cl_finish(p, L, aux, tid, q);
 }

@@ -117,9 +117,7 @@ struct Params {
 struct WsLayout {
   size_t ctrl, slot_expert, coef, gate, logits, himg, himg_stride, hinv, ximg, xinv, partial, facc, total;
 };
-// CTRL_FCOUNT + q: CTAs of the cluster kernel that have added their partial sums to output half q
-// (back at zero after every call)
-enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_FCOUNT = 6, CTRL_WORDS = 16 };
+enum : int { CTRL_ROUTE_COUNT = 0, CTRL_STATUS = 4, CTRL_NSLOTS = 5, CTRL_WORDS = 16 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -1320,7 +1318,11 @@ int launch_moe(const moe::Params& p, cudaStream_t stream) {
       set_error(std::string("moe cluster launch: ") + cudaGetErrorString(err));
       return 2;
     }
-    note_launches(2);
+    const int pairs = p.T * p.H / 2;
+    if (int rc = launch_one(moe::finish_kernel, (pairs + moe::kFinishThreads - 1) / moe::kFinishThreads,
+                            moe::kFinishThreads, 0, stream, "moe finish", p))
+      return rc;
+    note_launches(3);
     return 0;
   }
   if (p.mode == 1) {

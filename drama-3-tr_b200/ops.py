@@ -145,6 +145,16 @@ def fp8_gemv(x: Tensor, q: Tensor, s: Tensor, bias: Optional[Tensor] = None, out
     return y
 
 
+def gemv_status(device=None) -> int:
+    """Reads and clears the tensor-core GEMV's status word on the current device (synchronises)."""
+    st = ctypes.c_uint32(0)
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    rc = _lib.load().dm3_gemv_status(ctypes.byref(st), _stream(dev))
+    if rc not in (_lib.DM3_OK, _lib.DM3_ETIMEOUT):
+        _lib.check(rc, "dm3_gemv_status")
+    return int(st.value)
+
+
 @fp8_gemv.register_fake
 def _(x, q, s, bias=None, out_fp32=False):
     return x.new_empty((x.shape[0], q.shape[0]), dtype=torch.float32 if out_fp32 else BF16)

@@ -64,6 +64,13 @@ int dm3_fp8_gemv(const void* x, int M, int K, int N, const void* q, int64_t ldq,
                  int srows, const void* bias, int bias_kind, void* y, int64_t ldy, int y_fp32, void* stream);
 
 /*
+ * Reads and clears the sticky status word of the tensor-core GEMV on the current device
+ * (synchronises the stream): bit 0 = a bounded wait ran out in some launch since the last read.
+ * Returns DM3_ETIMEOUT in that case, DM3_OK otherwise. The reference has no counterpart.
+ */
+int dm3_gemv_status(uint32_t* status, void* stream);
+
+/*
  * Gathered block-FP8 GEMV: as dm3_fp8_gemv, but output row n reads weight row rows[n] of q
  * (and its scale row rows[n] / srows). Covers the audio head restricted to the eos token plus
  * the semantic band, `lm_head.weight[candidates]` (engine.py:409-411), without materialising
