@@ -426,15 +426,17 @@ __global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_con
   }
   __syncthreads();
   if (warp == 0) {
-    uint64_t k8[8];
+    // theta = the K-th largest of the 32 lane maxima of the lower bounds: at most the K-th largest
+    // lower bound, so the candidate set below only grows (by a few experts) and still holds every
+    // expert that can be selected; it costs one round of 32 shuffles instead of a full top-8 merge
+    uint64_t mk = 0ull;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) k8[i] = sm.keys[lane + 32 * i];
-    warp_top8(k8);
-    uint64_t kth = k8[0];
+    for (int i = 0; i < 8; ++i) mk = max(mk, sm.keys[lane + 32 * i]);
+    int beats = 0;
 #pragma unroll
-    for (int j = 1; j < 8; ++j)
-      if (j == K - 1) kth = k8[j];
-    if (lane == 0) sm.theta = key_value(static_cast<uint32_t>(kth >> 32));
+    for (int j = 0; j < 32; ++j) beats += __shfl_sync(0xffffffffu, mk, j) > mk ? 1 : 0;
+    const unsigned who = __ballot_sync(0xffffffffu, beats == K - 1);
+    if (lane == __ffs(who) - 1) sm.theta = key_value(static_cast<uint32_t>(mk >> 32));
   }
   __syncthreads();
   // candidate list (ascending expert order), then the shared gate row
@@ -497,20 +499,42 @@ __global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_con
   if (warp != 0) return;
   // selection among the candidates (exact values), softmax over all, renormalise
   float fx[8];
-  uint64_t k[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = lane + 32 * i;
     fx[i] = e < E ? sm.fx[e] : -FLT_MAX;
-    k[i] = (e < E && sm.is_cand[e]) ? (static_cast<uint64_t>(order_key(fx[i])) << 32) | static_cast<uint32_t>(~e) : 0ull;
   }
-  warp_top8(k);
   int sel_e[8];
   float sel_v[8];
+  const int nr = nc - (gate_row ? 1 : 0);  // routed candidates, in ascending expert order
+  if (nr <= 32) {
+    // lane c ranks candidate c by counting the larger keys: the order of the top-8 merge (exact
+    // logit descending, ties to the lower expert); the selections are the ranks below K
+    const int ce = lane < nr ? sm.cand[lane] : 0;
+    const uint64_t ck = lane < nr ? (static_cast<uint64_t>(order_key(sm.fx[ce])) << 32) | static_cast<uint32_t>(~ce) : 0ull;
+    int rank = 0;
+    for (int j = 0; j < nr; ++j) rank += __shfl_sync(0xffffffffu, ck, j) > ck ? 1 : 0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    sel_e[j] = static_cast<int>(~static_cast<uint32_t>(k[j]));
-    sel_v[j] = key_value(static_cast<uint32_t>(k[j] >> 32));
+    for (int j = 0; j < 8; ++j) {
+      const unsigned who = __ballot_sync(0xffffffffu, lane < nr && rank == j);
+      const int src = who ? __ffs(who) - 1 : 0;
+      const uint64_t kj = __shfl_sync(0xffffffffu, ck, src);
+      sel_e[j] = who ? static_cast<int>(~static_cast<uint32_t>(kj)) : 0;
+      sel_v[j] = who ? key_value(static_cast<uint32_t>(kj >> 32)) : -FLT_MAX;
+    }
+  } else {
+    uint64_t k[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int e = lane + 32 * i;
+      k[i] = (e < E && sm.is_cand[e]) ? (static_cast<uint64_t>(order_key(fx[i])) << 32) | static_cast<uint32_t>(~e) : 0ull;
+    }
+    warp_top8(k);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      sel_e[j] = static_cast<int>(~static_cast<uint32_t>(k[j]));
+      sel_v[j] = key_value(static_cast<uint32_t>(k[j] >> 32));
+    }
   }
   const float m = sel_v[0];
   float z = 0.f;
