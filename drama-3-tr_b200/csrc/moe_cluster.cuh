@@ -15,8 +15,9 @@
 //   down  output rows [qH/2, qH/2 + H/2) against the quarter's 128 columns of h (split-K over the
 //         quarters). These weights do not depend on h, so they stream through the same ring right
 //         behind the up slabs and are already in shared memory when h arrives;
-//   sum   every output element's contribution is added as a 64-bit fixed-point integer (2^-36
-//         units) into the workspace with a reduction in L2: integer addition is exact and
+//   sum   every output element's contribution is added as a 64-bit fixed-point integer (units
+//         of 2^-u per row, u from the row's magnitude) into the workspace with a reduction in L2:
+//         integer addition is exact and
 //         associative, so the sum does not depend on arrival order (deterministic). For each half
 //         of the output rows, the CTA that counts last converts its sums to y with the reference's
 //         rounding points and clears them.
@@ -39,7 +40,14 @@ constexpr uint32_t kFTmemCols = 512;
 constexpr int kBarGate = 4;             // named barrier of the 64 gate-row threads (warps 4-5)
 constexpr int kHxRows = 8;              // B rows of h sent: hi of rows 0-3, lo of rows 0-3
 constexpr uint32_t kHxBytesPerSrc = kHxRows * kUpHalf + 16;  // h bytes + the exponent vector
-constexpr float kFixScale = 68719476736.0f;                  // 2^36 fixed-point units per 1.0
+// Fixed-point unit of row t: 2^-u_t with u_t = 22 + 2 e_t, e_t the row's split exponent (x * 2^e_t
+// has its maximum in [128, 256)). A layer's output scales as |x|^2 (h = silu(gate x) * up x), so the
+// sums keep about 30 significant bits whatever the rows' magnitude: u = 34 for RMS-normalised rows
+// (maximum ~3.5), larger for tiny rows, smaller for rows with large outliers.
+__device__ __forceinline__ int fix_exponent(float xmax) {
+  const int u = 22 + 2 * split_exponent(xmax);
+  return u < -60 ? -60 : (u > 100 ? 100 : u);
+}
 constexpr int kTableThreads = kThreads - 64;                  // the table barrier: all warps but 2-3
 
 // Barriers and small state of the cluster kernel.
@@ -53,6 +61,7 @@ struct FAux {
   int epi_ok[4];
   int n_slots;
   float xinv[kMaxT];
+  float fixu[kMaxT];                  // 2^u_t: fixed-point units per 1.0 of row t
   float upv[kUpHalf][kMaxT];
   uint32_t hmax[2][kMaxT];            // |h| maxima of the two gate warps
   uint32_t xmax[kMaxT];               // |x| maxima (float bits) of the x split
@@ -396,7 +405,7 @@ __device__ __forceinline__ void cl_epilogue_down(const Params& p, const WsLayout
       if (b < nb) {
         const float y = sc[b] * fmaf(h0, v[b][0][t] + v[b][0][4 + t], h1 * (v[b][1][t] + v[b][1][4 + t])) * cf;
         atomicAdd(fa + static_cast<size_t>(t) * p.H + kBlockRows * b,
-                  static_cast<unsigned long long>(__float2ll_rn(y * kFixScale)));
+                  static_cast<unsigned long long>(__float2ll_rn(y * aux.fixu[t])));
       }
   }
 }
@@ -404,7 +413,7 @@ __device__ __forceinline__ void cl_epilogue_down(const Params& p, const WsLayout
 // The fixed-point sums to y, after the cluster kernel has completed: one thread per pair of output
 // elements, with the rounding points of combine_kernel,
 // y = bf16(bf16(bf16(routed) + bias) + bf16(sigmoid gate * bf16(shared))); the sums are cleared for
-// the next call. A sum converts to fp32 with one rounding (int64 -> float, then an exact 2^-36).
+// the next call. A sum converts to fp32 with one rounding (int64 -> float, then an exact 2^-u).
 // Kernel completion orders every CTA's reductions before these loads, so the cluster kernel needs
 // no fence, counter or last-CTA step of its own; the bias is requested before griddepcontrol.wait.
 // (Releasing the next layer's route kernel at this kernel's entry, so that it fetches its router
@@ -435,7 +444,7 @@ __global__ void __launch_bounds__(kFinishThreads) finish_kernel(const __grid_con
     S = __ldcg(reinterpret_cast<const longlong2*>(fa + shared_off + off));
     g = __ldcg(reinterpret_cast<const float*>(p.ws + L.gate) + t);
   }
-  const float unit = 1.0f / kFixScale;
+  const float unit = __ldcg(reinterpret_cast<const float*>(p.ws + L.xinv) + t);
   float y0 = bf16_round(__ll2float_rn(R.x) * unit), y1 = bf16_round(__ll2float_rn(R.y) * unit);
   if (p.out_bias) {
     y0 = bf16_round(y0 + b0);
@@ -491,7 +500,15 @@ __device__ void cl_split_x(const Params& p, uint8_t* bt, FAux& aux, int sidx) {
     if ((sidx & 31) == 0) atomicMax(&aux.xmax[t], wm);
   }
   named_bar(kBarSplit, kNT);
-  if (sidx < kMaxT) aux.xinv[sidx] = exp2i(-split_exponent(__uint_as_float(aux.xmax[sidx])));
+  if (sidx < kMaxT) {
+    const float am = __uint_as_float(aux.xmax[sidx]);
+    aux.xinv[sidx] = exp2i(-split_exponent(am));
+    aux.fixu[sidx] = exp2i(fix_exponent(am));
+    // the finish kernel converts the sums with the inverse unit (the x-split slot of the workspace is
+    // free on this path)
+    if (blockIdx.x == 0 && sidx < p.T)
+      reinterpret_cast<float*>(p.ws + ws_layout(p.H, p.I).xinv)[sidx] = exp2i(-fix_exponent(am));
+  }
 #pragma unroll
   for (int q = 0; q < kMaxTasks; ++q) {
     const int task = sidx + q * kNT;
