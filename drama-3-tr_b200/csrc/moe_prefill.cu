@@ -52,7 +52,7 @@ constexpr int kSlab = kRows * 128;           // one 128-byte K slab of a 128-row
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
 __host__ __device__ constexpr int epi_groups(bool down) { return down ? 1 : 2; }
-__host__ __device__ constexpr int expert_threads(bool down) { return 64 + epi_groups(down) * kEpiThreads; }
+__host__ __device__ constexpr int expert_threads(bool down) { return 96 + epi_groups(down) * kEpiThreads; }
 constexpr int kStages = 4;                   // ring of TMA stages
 constexpr int kStage = 3 * kSlab;            // two weight slabs, the activation slab (<= 128 rows)
 constexpr int kNacc = 2;                     // TMEM accumulator buffers of 256 columns
@@ -931,7 +931,7 @@ struct Aux {
   // item before group g's next one, so no group waits on an accumulator barrier more than one
   // phase ahead of the MMAs
   uint64_t turn[2];
-  uint64_t mma_done;
+  uint64_t mma_done, mma_done2;
   uint32_t tmem;
   int abort;
   int last;  // expert parallel, down: this CTA finished last
@@ -994,6 +994,7 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
     mbar_init(&aux.turn[0], kEpiWarps);
     mbar_init(&aux.turn[1], kEpiWarps);
     mbar_init(&aux.mma_done, 1);
+    mbar_init(&aux.mma_done2, 1);
     aux.abort = 0;
     fence_mbar_init();
   }
@@ -1046,8 +1047,10 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
       for (int s = max(0, total - kStages); s < total; ++s) mbar_wait(&aux.full[s % kStages], (s / kStages) & 1);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ================================================================ MMA issuer (lane 0)
+  } else if (warp == 1 || warp == expert_threads(DOWN) / 32 - 1) {
+    // ================================================================ MMA issuers (lane 0): warp 1 the
+    // even accumulator uses (buffer 0), the last warp the odd ones (buffer 1)
+    const int par = warp == 1 ? 0 : 1;
     if (lane == 0) {
       int s = 0, use = 0;
       for (int k = 0; k < my_items; ++k) {
@@ -1055,6 +1058,7 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
         const uint32_t idesc = tc::idesc_e4m3(kRows, 16 << box_index(it.z));
         for (int kb = 0; kb < nkb; ++kb, ++s, ++use) {
           const int ab = use % kNacc;
+          if (ab != par) continue;
           wait_or_abort(p, &aux.acc_empty[ab], ((use / kNacc) & 1) ^ 1u, abort);
           wait_or_abort(p, &aux.full[s % kStages], (s / kStages) & 1, abort);
           tc::fence_after_sync();
@@ -1070,8 +1074,8 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
           tc::mma_commit(&aux.acc_full[ab]);
         }
       }
-      tc::mma_commit(&aux.mma_done);
-      wait_or_abort(p, &aux.mma_done, 0, abort);
+      tc::mma_commit(par ? &aux.mma_done2 : &aux.mma_done);
+      wait_or_abort(p, par ? &aux.mma_done2 : &aux.mma_done, 0, abort);
     }
     __syncwarp();
   } else {
