@@ -900,7 +900,7 @@ def run_gemv(args, world, rank, local):
             "config": {"workload": "gemv_sweep_m2", "copies": copies, "value_shape": main_key,
                        "l2": "no flush: 40 distinct weight copies per graph, each launch reads cold rows"},
             "roofline": {"bound": "hbm", "achieved": res[main_key]["GBps"], "peak": hbm, "unit": "GB/s",
-                         "frac": res[main_key]["frac"], "kernel": "dm3::gemv_tc::gemv_tc_kernel, 2048x4096",
+                         "frac": res[main_key]["frac"], "kernel": "dm3::gemv::gemv_kernel<1> (FP8 mma.sync on raw e4m3 rows), 2048x4096",
                          "traffic": None},
             "shapes": res, "gpu_launches": args.steps * copies * 11}
 

@@ -1,34 +1,46 @@
-// Block-FP8 GEMV for B200 (sm_100a): y[M, N] = x[M, K] * dequant(q[N, K])^T, M <= 4.
+// Block-FP8 GEMV for B200 (sm_100a): y[M, N] = x[M, K] * dequant(q[N, K])^T (+ bias), M <= 4.
 //
-// Each CTA owns a contiguous, balanced range of output rows (one CTA per SM). A producer warp
-// streams tiles of up to 16 weight rows into a 2-stage shared-memory ring with cp.async.bulk
-// (one copy per tile when the rows are contiguous, one per row for a gathered head) together with
-// the tile's scale rows; 8 consumer warps split the K blocks of a tile and run FP8 m16n8k32
-// mma.sync on the raw e4m3 bytes against the exact e4m3 hi/lo split of x.
-// Per 128-wide K block the fp32 partial is multiplied by its block scale, as the reference
-// Triton kernel does (fp8_linear.py:21-26).
-//
-// Programmatic dependent launch: the weight copies of the first tiles are issued before
-// griddepcontrol.wait (weights are never produced by the preceding kernel), so a chain of
-// GEMVs in a CUDA graph overlaps each kernel's DRAM ramp-up with the previous one's tail.
+// A decode GEMV moves N x K weight bytes once and does 2 M flops per byte: it is bound by HBM and
+// by the latency of its short dependent chain, not by arithmetic.
+// * One CTA per SM owns a balanced range of output rows. A producer warp copies them, 16 rows x
+//   2048 bytes of K per stage, into a shared-memory ring with cp.async.bulk (one copy per row, at a
+//   padded pitch so that fragment loads are free of bank conflicts), starting before
+//   griddepcontrol.wait: weights are never produced by the preceding kernel, so a chain of GEMVs
+//   streams each call's weights beside the previous call.
+// * After the wait, each of 8 consumer warps splits its two 128-wide K blocks (per 2048-byte chunk)
+//   of the M <= 4 rows of x exactly into e4m3 hi + lo (power-of-two prescale per row and K block),
+//   then multiplies the raw e4m3 weight rows by them with the FP8 mma.sync m16n8k32 (16 weight rows
+//   x 8 columns: hi of rows 0-3, lo of rows 0-3): four MMAs per K block and 16 rows. (Widening every
+//   weight byte e4m3 -> f16 -> f32 on the CUDA cores and using packed fp32 FMAs measured 1.6x slower
+//   at 2048 x 4096: the conversions are low-throughput instructions.) Each K block's fp32 partial is
+//   scaled by its block scale, as the reference Triton kernel does (fp8_linear.py:21-26).
+// * The warps' partials of a row are added in a fixed order, so results do not depend on timing.
+// * A gathered row list (the audio head's rows of the full vocabulary matrix) only changes the
+//   source address of each row copy.
 #include "dm3_common.cuh"
 #include "dm3_internal.h"
 
 namespace dm3 {
 namespace gemv {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
-constexpr int kStages = 2;
-constexpr int kPad = 64;
+constexpr int kWarps = 8;                    // consumer warps
+constexpr int kThreads = (kWarps + 1) * 32;  // + the producer warp
+constexpr int kTileRows = 16;
+constexpr int kChunk = 2048;                 // bytes of K per stage (16 blocks: 2 per warp)
+constexpr int kPitch = kChunk + 64;          // row pitch of a stage: rows g, g + 1 64 bytes apart mod 128
+constexpr int kStageBytes = kTileRows * kPitch;
+constexpr int kRingSlots = 3;
+constexpr int kMaxRows = 64;                 // rows per CTA; larger N takes more CTAs than SMs
+constexpr int kSmemBudget = 115200;          // two CTAs (this call and the next of a chain) per SM
+
+static __device__ uint32_t g_status;
 
 struct Params {
   const __nv_bfloat16* x;
   int M, K, N;
   const uint8_t* q;
   int64_t ldq;
-  const int64_t* rows;  // optional gather list [N]
+  const int64_t* rows;  // optional gather list [N] (a parameter: read before griddepcontrol.wait)
   int64_t n_rows_q;
   const float* s;
   int64_t lds;
@@ -38,36 +50,9 @@ struct Params {
   void* y;
   int64_t ldy;
   int y_fp32;
-  int tile_rows;  // rows per stage (<= 16)
-  int sc_bulk;    // scale rows staged by bulk copy (16-byte aligned rows); else read from global
-};
-
-struct Smem {
-  int pitch, stage_bytes, stage, xq, red, misc, total;
-};
-
-__host__ __device__ inline Smem smem_layout(int K, int tile_rows) {
-  Smem S;
-  S.pitch = K + kPad;  // activation columns (thread-written, padded); weight rows are unpadded
-  const int sb = tile_rows * K + tile_rows * (K / 128) * 4;
-  S.stage_bytes = (sb + 127) / 128 * 128;
-  int o = 0;
-  S.stage = o;
-  o += kStages * S.stage_bytes;
-  S.xq = o;
-  o += 8 * S.pitch;
-  S.red = o;
-  o += kConsumerWarps * 16 * 4 * 4;
-  S.misc = o;
-  o += 256;
-  S.total = o;
-  return S;
-}
-
-struct Misc {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  float xinv[kMaxT];
+  int nch;    // 2048-byte chunks of K
+  int slots;  // ring slots
+  int off_sc, off_red, off_bar;
 };
 
 __device__ __forceinline__ int64_t src_row(const Params& p, int r) {
@@ -79,183 +64,240 @@ __device__ __forceinline__ int64_t src_row(const Params& p, int r) {
   return v;
 }
 
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const Params p) {
+template <int NCH>
+__global__ void __launch_bounds__(kThreads, NCH <= 2 ? 2 : 1) gemv_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const Smem S = smem_layout(p.K, p.tile_rows);
-  Misc* misc = reinterpret_cast<Misc*>(smem + S.misc);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
+  uint64_t* empty = full + kRingSlots;
+  float* sc = reinterpret_cast<float*>(smem + p.off_sc);
+  float* red = reinterpret_cast<float*>(smem + p.off_red);  // [tile][warp][16 rows][4 x rows]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row_begin = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.N) / gridDim.x);
   const int row_end = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.N) / gridDim.x);
-  const int TR = p.tile_rows;
-  const int n_tiles = (row_end - row_begin + TR - 1) / TR;
-  const int nkb = p.K / 128;
+  const int R = row_end - row_begin;
+  const int n_tiles = (R + kTileRows - 1) / kTileRows;
+  const int n_stages = n_tiles * p.nch;
+  const int nkb = p.K >> 7;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&misc->full[s], 1);
-      mbar_init(&misc->empty[s], kConsumerWarps);
+    for (int i = 0; i < p.slots; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kWarps);
     }
     fence_mbar_init();
   }
   __syncthreads();
   griddep_launch();
 
-  if (warp == kConsumerWarps) {
+  if (warp == kWarps) {
     // ---------------------------------------------------------------- producer
-    // Weights do not depend on the preceding kernel, so copies start before griddepcontrol.wait.
-    uint32_t empty_par = 1;
-    const bool contiguous = p.rows == nullptr && p.ldq == p.K;
-    for (int i = 0; i < n_tiles; ++i) {
-      const int stage = i % kStages;
-      if (i > 0 && stage == 0) empty_par ^= 1u;
-      bool ok = true;
-      if (lane == 0) ok = mbar_wait(&misc->empty[stage], empty_par);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;  // consumers gone: nothing more can be delivered
-      const int r0 = row_begin + i * TR;
-      const int nr = min(TR, row_end - r0);
-      uint8_t* st = smem + S.stage + stage * S.stage_bytes;
-      uint64_t* full = &misc->full[stage];
-      float* sd = reinterpret_cast<float*>(st + TR * p.K);
-      const uint32_t srow = nkb * 4;
-      // scale rows: 1x128 with contiguous rows -> one copy; 128x128 -> the (at most two) block rows
-      // at positions 0, 1; gathered rows -> one copy per row
-      const bool sc_one = p.sc_bulk && p.srows == 1 && p.rows == nullptr && p.lds == nkb;
-      const bool sc_blk = p.sc_bulk && p.srows == 128 && p.rows == nullptr;
-      const int sb0 = r0 / 128, sb1 = (r0 + nr - 1) / 128;
-      uint32_t sbytes = 0;
-      if (p.sc_bulk) sbytes = sc_one ? nr * srow : (sc_blk ? (sb1 - sb0 + 1) * srow : nr * srow);
-      if (lane == 0) {
-        mbar_arrive_expect_tx(full, static_cast<uint32_t>(nr * p.K) + sbytes);
-        if (contiguous) bulk_g2s(st, p.q + static_cast<int64_t>(r0) * p.K, nr * p.K, full);
-        if (sc_one) {
-          bulk_g2s(sd, p.s + static_cast<int64_t>(r0) * nkb, nr * srow, full);
-        } else if (sc_blk) {
-          for (int b = sb0; b <= sb1; ++b) bulk_g2s(sd + (b - sb0) * nkb, p.s + static_cast<int64_t>(b) * p.lds, srow, full);
+    for (int i = 0; i < n_stages; ++i) {
+      const int slot = i % p.slots;
+      if (i >= p.slots) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&empty[slot], ((i / p.slots) - 1) & 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
+          break;  // the consumers are gone: nothing more can be delivered
         }
       }
+      const int t = i / p.nch, c = i - t * p.nch;
+      const int r0 = row_begin + t * kTileRows;
+      const int nr = min(kTileRows, row_end - r0);
+      const int k0 = c * kChunk;
+      const int kc = min(kChunk, p.K - k0);
+      uint8_t* dst = smem + slot * kStageBytes;
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nr * kc));
       __syncwarp();
-      if (lane < nr) {
-        const int64_t src = src_row(p, r0 + lane);
-        if (!contiguous) bulk_g2s(st + lane * p.K, p.q + src * p.ldq, p.K, full);
-        if (p.sc_bulk && !sc_one && !sc_blk)
-          bulk_g2s(sd + lane * nkb, p.s + (src / p.srows) * p.lds, srow, full);
-      }
+      if (lane < nr) bulk_g2s(dst + lane * kPitch, p.q + src_row(p, r0 + lane) * p.ldq + k0, kc, &full[slot]);
     }
-  } else {
-    // ---------------------------------------------------------------- consumers
-    griddep_wait();  // x is produced by the preceding kernel
-    uint8_t* xq = smem + S.xq;
-    if (warp < p.M) {
-      const __nv_bfloat16* xr = p.x + static_cast<size_t>(warp) * p.K;
-      float amax = 0.f;
-      for (int k = lane * 8; k < p.K; k += 256) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  // the scales of this CTA's rows (parameters, like the weights)
+  for (int i = tid; i < R * nkb; i += kWarps * 32) {
+    const int r = i / nkb, kb = i - r * nkb;
+    sc[i] = __ldg(p.s + (src_row(p, row_begin + r) / p.srows) * p.lds + kb);
+  }
+  const int g = lane >> 2, q = lane & 3;
+  // split x into this warp's B fragments: K blocks c * 16 + 2 * warp + i of every chunk c.
+  // The split goes through this warp's 1 KB of the (not yet used) partial-sum area.
+  uint8_t* xw = reinterpret_cast<uint8_t*>(red) + warp * 1024;
+  griddep_wait();  // x is produced by the preceding kernel
+  uint4 bfr[NCH][2][2];
+  float ef[NCH][2][2];  // inverse prescale of this lane's two x rows, per K block
+  {
+    const bool two = p.M <= 2;
+    const int m = two ? lane >> 4 : lane >> 3;       // x row this lane splits
+    const int cw = two ? 8 : 16;                     // values per lane
+    const int c0 = (two ? (lane & 15) : (lane & 7)) * cw;
+    // every load first: one memory round trip for all of the warp's K blocks
+    uint4 raw[NCH][2][2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(e[i])));
+    for (int c = 0; c < NCH; ++c)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int kb = c * 16 + 2 * warp + i;
+        raw[c][i][0] = raw[c][i][1] = make_uint4(0u, 0u, 0u, 0u);
+        if (kb < nkb && m < p.M) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(m) * p.K + kb * 128 + c0);
+          raw[c][i][0] = src[0];
+          if (!two) raw[c][i][1] = src[1];
+        }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-      const int e = split_exponent(amax);
-      const float sc = exp2i(e);
-      if (lane == 0) misc->xinv[warp] = exp2i(-e);
-      uint8_t* hi = xq + warp * S.pitch;
-      uint8_t* lo = xq + (4 + warp) * S.pitch;
-      for (int k = lane * 8; k < p.K; k += 256) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&v);
-        uint16_t h4[4], l4[4];
+    for (int c = 0; c < NCH; ++c)
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          split2(__bfloat162float(e8[2 * i]) * sc, __bfloat162float(e8[2 * i + 1]) * sc, h4[i], l4[i]);
-        *reinterpret_cast<uint2*>(hi + k) =
-            make_uint2(h4[0] | (uint32_t(h4[1]) << 16), h4[2] | (uint32_t(h4[3]) << 16));
-        *reinterpret_cast<uint2*>(lo + k) =
-            make_uint2(l4[0] | (uint32_t(l4[1]) << 16), l4[2] | (uint32_t(l4[3]) << 16));
-      }
-    }
-    named_bar(1, kConsumers);
-    const int g = lane >> 2, q = lane & 3;
-    const bool bvalid = (g & 3) < p.M;
-    const uint8_t* bcol = xq + g * S.pitch;
-    float* red = reinterpret_cast<float*>(smem + S.red);
-    uint32_t full_par = 0;
-    for (int i = 0; i < n_tiles; ++i) {
-      const int stage = i % kStages;
-      if (i > 0 && stage == 0) full_par ^= 1u;
-      if (!mbar_wait(&misc->full[stage], full_par)) break;
-      const int r0 = row_begin + i * TR;
-      const int nr = min(TR, row_end - r0);
-      const uint8_t* st = smem + S.stage + stage * S.stage_bytes;
-      const float* sc = reinterpret_cast<const float*>(st + TR * p.K);
-      const bool lo_ok = g < nr, hi_ok = g + 8 < nr;
-      const uint8_t* row_lo = st + g * p.K;
-      const uint8_t* row_hi = st + (g + 8) * p.K;
-      // where each of this lane's two rows finds its scale row
-      const bool sc_blk = p.srows == 128 && p.rows == nullptr;
-      int si_lo = g, si_hi = g + 8;
-      if (sc_blk) {
-        si_lo = (r0 + g) / 128 - r0 / 128;
-        si_hi = (r0 + g + 8) / 128 - r0 / 128;
-      }
-      const float* gs_lo = p.s + (lo_ok ? (src_row(p, r0 + g) / p.srows) * p.lds : 0);
-      const float* gs_hi = p.s + (hi_ok ? (src_row(p, r0 + g + 8) / p.srows) * p.lds : 0);
-      float tot[4] = {0.f, 0.f, 0.f, 0.f};
-      // this warp's k blocks: warp, warp + 8, ...; two per pass, all fragments loaded up front
-      for (int kb0 = warp; kb0 < nkb; kb0 += 2 * kConsumerWarps) {
-        const int kb1 = kb0 + kConsumerWarps;
-        const bool v1 = kb1 < nkb;
-        const int kbs[2] = {kb0, v1 ? kb1 : kb0};
-        float part[2][4];
-        tile_kblocks<2>(part, row_lo, row_hi, bcol, lo_ok, hi_ok, bvalid, kbs, q);
+      for (int i = 0; i < 2; ++i) {
+        const int kb = c * 16 + 2 * warp + i;
+        const bool kv = kb < nkb;
+        float v[16];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          float s0 = 0.f, s1 = 0.f;
-          if (i == 0 || v1) {
-            if (p.sc_bulk) {
-              if (lo_ok) s0 = sc[si_lo * nkb + kbs[i]];
-              if (hi_ok) s1 = sc[si_hi * nkb + kbs[i]];
-            } else {
-              if (lo_ok) s0 = __ldg(gs_lo + kbs[i]);
-              if (hi_ok) s1 = __ldg(gs_hi + kbs[i]);
+        for (int e = 0; e < 16; ++e) v[e] = 0.f;
+        if (kv && m < p.M) {
+          const uint4 u0 = raw[c][i][0];
+          const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            v[2 * e] = __uint_as_float(w0[e] << 16);
+            v[2 * e + 1] = __uint_as_float(w0[e] & 0xffff0000u);
+          }
+          if (!two) {
+            const uint4 u1 = raw[c][i][1];
+            const uint32_t w1[4] = {u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              v[8 + 2 * e] = __uint_as_float(w1[e] << 16);
+              v[8 + 2 * e + 1] = __uint_as_float(w1[e] & 0xffff0000u);
             }
           }
-          tot[0] = fmaf(part[i][0], s0, tot[0]);
-          tot[1] = fmaf(part[i][1], s0, tot[1]);
-          tot[2] = fmaf(part[i][2], s1, tot[2]);
-          tot[3] = fmaf(part[i][3], s1, tot[3]);
         }
-      }
+        float amax = 0.f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) tot[j] += __shfl_down_sync(0xffffffffu, tot[j], 2);
-      if (q < 2) {
-        float* rw = red + warp * 64;
-        rw[g * 4 + 2 * q] = tot[0];
-        rw[g * 4 + 2 * q + 1] = tot[1];
-        rw[(g + 8) * 4 + 2 * q] = tot[2];
-        rw[(g + 8) * 4 + 2 * q + 1] = tot[3];
-      }
-      named_bar(1, kConsumers);
-      if (tid < 64) {
-        const int r = tid >> 2, t = tid & 3;
-        if (r < nr && t < p.M) {
-          float v = 0.f;
+        for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
+        // the lanes holding the same x row of this K block
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        if (two) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 8));
+        const int ex = split_exponent(amax);
+        const float pre = exp2i(ex);
+        uint32_t hi[4], lo[4];
 #pragma unroll
-          for (int w = 0; w < kConsumerWarps; ++w) v += red[w * 64 + r * 4 + t];
-          v *= misc->xinv[t];
-          const int n = r0 + r;
-          if (p.bias_kind == 1) v += __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
-          if (p.bias_kind == 2) v += static_cast<const float*>(p.bias)[n];
-          if (p.y_fp32)
-            static_cast<float*>(p.y)[t * p.ldy + n] = v;
-          else
-            static_cast<__nv_bfloat16*>(p.y)[t * p.ldy + n] = __float2bfloat16_rn(v);
+        for (int e = 0; e < 4; ++e) {
+          uint16_t h0, l0, h1, l1;
+          split2(v[4 * e] * pre, v[4 * e + 1] * pre, h0, l0);
+          split2(v[4 * e + 2] * pre, v[4 * e + 3] * pre, h1, l1);
+          hi[e] = h0 | (static_cast<uint32_t>(h1) << 16);
+          lo[e] = l0 | (static_cast<uint32_t>(l1) << 16);
         }
+        // columns: m = hi of x row m, 4 + m = lo; rows 2-3 stay zero when M <= 2
+        __syncwarp();
+        if (two) {
+          *reinterpret_cast<uint2*>(xw + m * 128 + c0) = make_uint2(hi[0], hi[1]);
+          *reinterpret_cast<uint2*>(xw + (4 + m) * 128 + c0) = make_uint2(lo[0], lo[1]);
+          *reinterpret_cast<uint2*>(xw + (2 + m) * 128 + c0) = make_uint2(0u, 0u);
+          *reinterpret_cast<uint2*>(xw + (6 + m) * 128 + c0) = make_uint2(0u, 0u);
+        } else {
+          *reinterpret_cast<uint4*>(xw + m * 128 + c0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          *reinterpret_cast<uint4*>(xw + (4 + m) * 128 + c0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        }
+        // inverse prescales of x rows 0-3 from the lanes that computed them
+        const float inv = exp2i(-ex);
+        const int src0 = (2 * (q & 1)) << (two ? 4 : 3), src1 = (2 * (q & 1) + 1) << (two ? 4 : 3);
+        const float i0 = __shfl_sync(0xffffffffu, inv, src0 & 31);
+        const float i1 = __shfl_sync(0xffffffffu, inv, src1 & 31);
+        ef[c][i][0] = (two && (q & 1)) ? 0.f : i0;
+        ef[c][i][1] = (two && (q & 1)) ? 0.f : i1;
+        __syncwarp();
+        bfr[c][i][0] = ld_smem16(xw + g * 128 + 16 * q);
+        bfr[c][i][1] = ld_smem16(xw + g * 128 + 64 + 16 * q);
       }
-      named_bar(1, kConsumers);
-      if (lane == 0) mbar_arrive(&misc->empty[stage]);
+  }
+  named_bar(1, kWarps * 32);  // scales visible; every warp is done with its split buffer
+
+  bool failed = false;
+  for (int i = 0; i < n_stages; ++i) {
+    const int slot = i % p.slots;
+    if (!failed) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[slot], (i / p.slots) & 1));
+      if (!ok) {
+        failed = true;
+        if (lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
+      }
     }
+    const int t = i / p.nch, c = i - t * p.nch;
+    if (!failed) {
+      const uint8_t* rlo = smem + slot * kStageBytes + g * kPitch;
+      const uint8_t* rhi = rlo + 8 * kPitch;
+      const int rl = min(t * kTileRows + g, R - 1), rh = min(t * kTileRows + g + 8, R - 1);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int cc = 0; cc < NCH; ++cc) {
+        if (cc != c) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int kbl = 2 * warp + j;  // K block within the chunk
+          const int kb = c * 16 + kbl;
+          if (kb < nkb) {
+            const uint4 a0 = ld_smem16(rlo + kbl * 128 + 16 * q), a1 = ld_smem16(rlo + kbl * 128 + 64 + 16 * q);
+            const uint4 h0 = ld_smem16(rhi + kbl * 128 + 16 * q), h1 = ld_smem16(rhi + kbl * 128 + 64 + 16 * q);
+            const uint4 b0 = bfr[cc][j][0], b1 = bfr[cc][j][1];
+            float t4[4][4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) t4[u][e] = 0.f;
+            mma_e4m3(t4[0], a0.x, h0.x, a0.y, h0.y, b0.x, b0.y);
+            mma_e4m3(t4[1], a0.z, h0.z, a0.w, h0.w, b0.z, b0.w);
+            mma_e4m3(t4[2], a1.x, h1.x, a1.y, h1.y, b1.x, b1.y);
+            mma_e4m3(t4[3], a1.z, h1.z, a1.w, h1.w, b1.z, b1.w);
+            const float sl = sc[rl * nkb + kb], sh = sc[rh * nkb + kb];
+            const float f00 = sl * ef[cc][j][0], f01 = sl * ef[cc][j][1];
+            const float f10 = sh * ef[cc][j][0], f11 = sh * ef[cc][j][1];
+            acc[0] = fmaf((t4[0][0] + t4[1][0]) + (t4[2][0] + t4[3][0]), f00, acc[0]);
+            acc[1] = fmaf((t4[0][1] + t4[1][1]) + (t4[2][1] + t4[3][1]), f01, acc[1]);
+            acc[2] = fmaf((t4[0][2] + t4[1][2]) + (t4[2][2] + t4[3][2]), f10, acc[2]);
+            acc[3] = fmaf((t4[0][3] + t4[1][3]) + (t4[2][3] + t4[3][3]), f11, acc[3]);
+          }
+        }
+      }
+      // hi (columns 2q, 2q + 1 for q < 2) + lo (the same x rows in lane q + 2)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 2);
+      if (q < 2) {
+        // chunk partials of a tile accumulate in place (chunks of a tile arrive in order)
+        float* rw = red + ((t * kWarps + warp) * kTileRows) * 4;
+        if (c == 0) {
+          *reinterpret_cast<float2*>(rw + g * 4 + 2 * q) = make_float2(acc[0], acc[1]);
+          *reinterpret_cast<float2*>(rw + (g + 8) * 4 + 2 * q) = make_float2(acc[2], acc[3]);
+        } else {
+          float2* a = reinterpret_cast<float2*>(rw + g * 4 + 2 * q);
+          float2* b = reinterpret_cast<float2*>(rw + (g + 8) * 4 + 2 * q);
+          *a = make_float2(a->x + acc[0], a->y + acc[1]);
+          *b = make_float2(b->x + acc[2], b->y + acc[3]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  named_bar(1, kWarps * 32);
+  for (int i = tid; i < R * p.M; i += kWarps * 32) {
+    const int m = i / R, r = i - m * R;
+    const int t = r / kTileRows, rr = r - t * kTileRows;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += red[((t * kWarps + w) * kTileRows + rr) * 4 + m];
+    const int n = row_begin + r;
+    if (p.bias_kind == 1) v += __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
+    if (p.bias_kind == 2) v += static_cast<const float*>(p.bias)[n];
+    if (p.y_fp32)
+      static_cast<float*>(p.y)[m * p.ldy + n] = v;
+    else
+      static_cast<__nv_bfloat16*>(p.y)[m * p.ldy + n] = __float2bfloat16_rn(v);
   }
 }
 
@@ -266,10 +308,47 @@ int launch_gemv_tc(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q
                    int64_t lds, int srows, const void* bias, int bias_kind, void* y, int64_t ldy, int y_fp32,
                    cudaStream_t stream);
 
+namespace {
+template <int NCH>
+cudaError_t launch_gemv_nch(const gemv::Params& p, int grid, int smem, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && !configured[dev]) {
+    e = cudaFuncSetAttribute(gemv::gemv_kernel<NCH>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(gemv::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemv::gemv_kernel<NCH>, p);
+}
+}  // namespace
+
 int launch_gemv(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q, int64_t ldq, const int64_t* rows,
                 int64_t n_rows_q, const float* s, int64_t lds, int srows, const void* bias, int bias_kind, void* y,
                 int64_t ldy, int y_fp32, cudaStream_t stream) {
-  gemv::Params p{};
+  using namespace gemv;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    set_error("cudaGetDevice failed");
+    return 2;
+  }
+  const int sms = sm_count(dev);
+  int grid = sms > (N + kMaxRows - 1) / kMaxRows ? sms : (N + kMaxRows - 1) / kMaxRows;
+  if (grid > N) grid = N;
+  const int max_rows = (N + grid - 1) / grid;
+  const int tiles = (max_rows + kTileRows - 1) / kTileRows;
+  Params p{};
   p.x = x;
   p.M = M;
   p.K = K;
@@ -286,42 +365,42 @@ int launch_gemv(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q, i
   p.y = y;
   p.ldy = ldy;
   p.y_fp32 = y_fp32;
-  p.tile_rows = K <= 2048 ? 16 : (K <= 4096 ? 8 : 4);
-  const int nkb = K / 128;
-  p.sc_bulk = (reinterpret_cast<uintptr_t>(s) & 15u) == 0 && (nkb * 4) % 16 == 0 && (lds * 4) % 16 == 0;
-  const gemv::Smem S = gemv::smem_layout(K, p.tile_rows);
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    set_error("cudaGetDevice failed");
-    return 2;
-  }
-  static bool configured[64] = {false};
-  if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(gemv::gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) !=
-        cudaSuccess) {
-      set_error("cudaFuncSetAttribute(gemv) failed");
-      return 2;
-    }
-    configured[dev] = true;
-  }
-  const int sms = sm_count(dev);
-  const int grid = N < sms ? N : sms;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(gemv::kThreads);
-  cfg.dynamicSmemBytes = S.total;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, gemv::gemv_kernel, p);
+  p.nch = (K + kChunk - 1) / kChunk;
+  const int stages = tiles * p.nch;
+  const int sc_bytes = (max_rows * (K / 128) * 4 + 15) / 16 * 16;
+  int red_bytes = tiles * kWarps * kTileRows * 4 * 4;
+  if (red_bytes < kWarps * 1024) red_bytes = kWarps * 1024;  // the split buffers share it
+  int slots = kRingSlots < stages ? kRingSlots : stages;
+  while (slots > 1 && slots * kStageBytes + sc_bytes + red_bytes + 2 * kRingSlots * 8 > kSmemBudget) --slots;
+  p.slots = slots;
+  int off = slots * kStageBytes;
+  p.off_sc = off;
+  off += sc_bytes;
+  p.off_red = off;
+  off += red_bytes;
+  p.off_bar = off;
+  off += 2 * kRingSlots * 8;
+  cudaError_t err;
+  if (p.nch == 1)
+    err = launch_gemv_nch<1>(p, grid, off, stream);
+  else if (p.nch == 2)
+    err = launch_gemv_nch<2>(p, grid, off, stream);
+  else
+    err = launch_gemv_nch<4>(p, grid, off, stream);
   if (err != cudaSuccess) {
     set_error(std::string("gemv launch: ") + cudaGetErrorString(err));
     return 2;
   }
   note_launches(1);
+  return 0;
+}
+
+// Reads and clears this file's status word (asynchronously on the stream).
+int gemv_status_async(uint32_t* host_value, cudaStream_t stream) {
+  const uint32_t zero = 0;
+  if (cudaMemcpyFromSymbolAsync(host_value, gemv::g_status, 4, 0, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaMemcpyToSymbolAsync(gemv::g_status, &zero, 4, 0, cudaMemcpyHostToDevice, stream) != cudaSuccess)
+    return 2;
   return 0;
 }
 
@@ -354,11 +433,15 @@ extern "C" int dm3_fp8_gemv(const void* x, int M, int K, int N, const void* q, i
   dm3::note_launches(0);
   const int rc = check_gemv(x, M, K, N, q, ldq, s, lds, srows, bias_kind, bias, y, ldy);
   if (rc) return rc;
-  // contiguous weight rows: the tensor-core kernel (split-K over a thread-block cluster)
-  const int rt = dm3::launch_gemv_tc(static_cast<const __nv_bfloat16*>(x), M, K, N, static_cast<const uint8_t*>(q),
-                                     ldq, s, lds, srows, bias, bias_kind, y, ldy, y_fp32,
-                                     static_cast<cudaStream_t>(stream));
-  if (rt >= 0) return rt;
+  // K <= 2048: this file's kernel (one 2048-byte chunk per row, measured faster on every such shape);
+  // longer rows: the tensor-core kernel (split-K over a thread-block cluster, gemv_tc.cu), which keeps
+  // its latency at K = 4096 and 8192 where a chunked row here costs more
+  if (K > 2048) {
+    const int rt = dm3::launch_gemv_tc(static_cast<const __nv_bfloat16*>(x), M, K, N, static_cast<const uint8_t*>(q),
+                                       ldq, s, lds, srows, bias, bias_kind, y, ldy, y_fp32,
+                                       static_cast<cudaStream_t>(stream));
+    if (rt >= 0) return rt;
+  }
   return dm3::launch_gemv(static_cast<const __nv_bfloat16*>(x), M, K, N, static_cast<const uint8_t*>(q), ldq,
                           nullptr, N, s, lds, srows, bias, bias_kind, y, ldy, y_fp32,
                           static_cast<cudaStream_t>(stream));

@@ -381,12 +381,14 @@ int wait_limit_gemv_tc(uint64_t ns) { return static_cast<int>(set_wait_limit_her
 extern "C" int dm3_gemv_status(uint32_t* status, void* stream) {
   if (!status) return dm3::set_error("null pointer argument"), 1;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint32_t v = 0;
+  uint32_t v = 0, v_cc = 0;
   const uint32_t zero = 0;
-  if (cudaMemcpyFromSymbolAsync(&v, dm3::gemv_tc::g_status, 4, 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+  if (dm3::gemv_status_async(&v_cc, s) != 0 ||
+      cudaMemcpyFromSymbolAsync(&v, dm3::gemv_tc::g_status, 4, 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
       cudaMemcpyToSymbolAsync(dm3::gemv_tc::g_status, &zero, 4, 0, cudaMemcpyHostToDevice, s) != cudaSuccess ||
       cudaStreamSynchronize(s) != cudaSuccess)
     return dm3::set_error("reading the GEMV status word failed"), 2;
+  v |= v_cc;
   *status = v;
   return (v & dm3::STATUS_TIMEOUT) ? 3 : 0;
 }
