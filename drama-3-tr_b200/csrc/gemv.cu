@@ -308,6 +308,38 @@ int launch_gemv_tc(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q
                    int64_t lds, int srows, const void* bias, int bias_kind, void* y, int64_t ldy, int y_fp32,
                    cudaStream_t stream);
 
+namespace gemv {
+// Grid, ring and shared-memory layout of a launch.
+struct Plan {
+  int grid, max_rows, nch, stages, slots, off_sc, off_red, off_bar, smem;
+};
+inline Plan plan_of(int K, int N, int sms) {
+  Plan P{};
+  P.grid = sms > (N + kMaxRows - 1) / kMaxRows ? sms : (N + kMaxRows - 1) / kMaxRows;
+  if (P.grid > N) P.grid = N;
+  P.max_rows = (N + P.grid - 1) / P.grid;
+  const int tiles = (P.max_rows + kTileRows - 1) / kTileRows;
+  P.nch = (K + kChunk - 1) / kChunk;
+  P.stages = tiles * P.nch;
+  const int sc_bytes = (P.max_rows * (K / 128) * 4 + 15) / 16 * 16;
+  int red_bytes = tiles * kWarps * kTileRows * 4 * 4;
+  if (red_bytes < kWarps * 1024) red_bytes = kWarps * 1024;  // the split buffers share it
+  P.slots = kRingSlots < P.stages ? kRingSlots : P.stages;
+  while (P.slots > 1 && P.slots * kStageBytes + sc_bytes + red_bytes + 2 * kRingSlots * 8 > kSmemBudget) --P.slots;
+  P.off_sc = P.slots * kStageBytes;
+  P.off_red = P.off_sc + sc_bytes;
+  P.off_bar = P.off_red + red_bytes;
+  P.smem = P.off_bar + 2 * kRingSlots * 8;
+  return P;
+}
+}  // namespace gemv
+
+// Every row of a CTA is one chunk of K and all of the CTA's stages fit the ring.
+bool gemv_rows_fit(int K, int N, int sms) {
+  const gemv::Plan P = gemv::plan_of(K, N, sms);
+  return P.nch == 1 && P.stages <= P.slots;
+}
+
 namespace {
 template <int NCH>
 cudaError_t launch_gemv_nch(const gemv::Params& p, int grid, int smem, cudaStream_t stream) {
@@ -343,11 +375,7 @@ int launch_gemv(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q, i
     set_error("cudaGetDevice failed");
     return 2;
   }
-  const int sms = sm_count(dev);
-  int grid = sms > (N + kMaxRows - 1) / kMaxRows ? sms : (N + kMaxRows - 1) / kMaxRows;
-  if (grid > N) grid = N;
-  const int max_rows = (N + grid - 1) / grid;
-  const int tiles = (max_rows + kTileRows - 1) / kTileRows;
+  const Plan P = plan_of(K, N, sm_count(dev));
   Params p{};
   p.x = x;
   p.M = M;
@@ -365,21 +393,12 @@ int launch_gemv(const __nv_bfloat16* x, int M, int K, int N, const uint8_t* q, i
   p.y = y;
   p.ldy = ldy;
   p.y_fp32 = y_fp32;
-  p.nch = (K + kChunk - 1) / kChunk;
-  const int stages = tiles * p.nch;
-  const int sc_bytes = (max_rows * (K / 128) * 4 + 15) / 16 * 16;
-  int red_bytes = tiles * kWarps * kTileRows * 4 * 4;
-  if (red_bytes < kWarps * 1024) red_bytes = kWarps * 1024;  // the split buffers share it
-  int slots = kRingSlots < stages ? kRingSlots : stages;
-  while (slots > 1 && slots * kStageBytes + sc_bytes + red_bytes + 2 * kRingSlots * 8 > kSmemBudget) --slots;
-  p.slots = slots;
-  int off = slots * kStageBytes;
-  p.off_sc = off;
-  off += sc_bytes;
-  p.off_red = off;
-  off += red_bytes;
-  p.off_bar = off;
-  off += 2 * kRingSlots * 8;
+  p.nch = P.nch;
+  p.slots = P.slots;
+  p.off_sc = P.off_sc;
+  p.off_red = P.off_red;
+  p.off_bar = P.off_bar;
+  const int grid = P.grid, off = P.smem;
   cudaError_t err;
   if (p.nch == 1)
     err = launch_gemv_nch<1>(p, grid, off, stream);
@@ -433,10 +452,13 @@ extern "C" int dm3_fp8_gemv(const void* x, int M, int K, int N, const void* q, i
   dm3::note_launches(0);
   const int rc = check_gemv(x, M, K, N, q, ldq, s, lds, srows, bias_kind, bias, y, ldy);
   if (rc) return rc;
-  // K <= 2048: this file's kernel (one 2048-byte chunk per row, measured faster on every such shape);
-  // longer rows: the tensor-core kernel (split-K over a thread-block cluster, gemv_tc.cu), which keeps
-  // its latency at K = 4096 and 8192 where a chunked row here costs more
-  if (K > 2048) {
+  // This file's kernel when every row of a CTA is one 2048-byte chunk and all of a CTA's rows fit its
+  // ring (all weights then arrive before griddepcontrol.wait returns): measured faster on every such
+  // shape. Otherwise the tensor-core kernel (split-K over a thread-block cluster, gemv_tc.cu), which
+  // keeps its latency at K = 4096 and 8192 and for 2048 x 8192.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return dm3::set_error("cudaGetDevice failed"), 2;
+  if (!dm3::gemv_rows_fit(K, N, dm3::sm_count(dev))) {
     const int rt = dm3::launch_gemv_tc(static_cast<const __nv_bfloat16*>(x), M, K, N, static_cast<const uint8_t*>(q),
                                        ldq, s, lds, srows, bias, bias_kind, y, ldy, y_fp32,
                                        static_cast<cudaStream_t>(stream));
