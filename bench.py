@@ -901,7 +901,7 @@ def run_gemv(args, world, rank, local):
                        "l2": "no flush: 40 distinct weight copies per graph, each launch reads cold rows"},
             "roofline": {"bound": "hbm", "achieved": res[main_key]["GBps"], "peak": hbm, "unit": "GB/s",
                          "frac": res[main_key]["frac"], "kernel": "dm3::gemv::gemv_kernel<1> (FP8 mma.sync on raw e4m3 rows), 2048x4096",
-                         "traffic": None},
+                         "traffic": recorded_traffic("gemv_2048x4096")},
             "shapes": res, "gpu_launches": args.steps * copies * 11}
 
 

@@ -459,6 +459,12 @@ __global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_con
   }
   __syncthreads();
   const int nc = sm.ncand;
+  double xd[8];  // this thread's x elements, exact in fp64 (converted once for every candidate)
+  {
+    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xd[j] = static_cast<double>(__bfloat162float(xe[j]));
+  }
   for (int c0 = 0; c0 < nc; c0 += kSelChunk) {
     uint4 wv[kSelChunk];
 #pragma unroll
@@ -470,18 +476,37 @@ __global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_con
         wv[c] = __ldg(reinterpret_cast<const uint4*>(wr + 8 * tid));
       }
     }
+    double a[kSelChunk];
 #pragma unroll
     for (int c = 0; c < kSelChunk; ++c) {
       const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[c]);
-      const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&xv);
-      double acc = 0.0;
+      a[c] = 0.0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        acc = fma(static_cast<double>(__bfloat162float(xe[j])), static_cast<double>(__bfloat162float(we[j])), acc);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) sm.part[warp][c] = acc;
+      for (int j = 0; j < 8; ++j) a[c] = fma(xd[j], static_cast<double>(__bfloat162float(we[j])), a[c]);
     }
+    // the 8 rows' sums over the warp by a transposing reduction: each halving step keeps half of the
+    // rows and sends the other half (9 shuffles of doubles instead of 40); lane l ends with row l / 4
+    static_assert(kSelChunk == 8, "the transposing reduction is written for 8 rows");
+    {
+      const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const double keep = u16 ? a[4 + i] : a[i], send = u16 ? a[i] : a[4 + i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const double keep = u8 ? a[2 + i] : a[i], send = u8 ? a[i] : a[2 + i];
+        a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+      }
+      {
+        const double keep = u4 ? a[1] : a[0], send = u4 ? a[0] : a[1];
+        a[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+      }
+      a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
+      a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
+    }
+    if ((lane & 3) == 0) sm.part[warp][lane >> 2] = a[0];
     __syncthreads();
     if (tid < kSelChunk && c0 + tid < nc) {
       double sum = 0.0;
@@ -573,9 +598,9 @@ __global__ void __launch_bounds__(kSelThreads, 4) select_kernel(const __grid_con
 // by expert (argsort(ids.flatten(), stable=True)): pair i of expert e goes to position
 // off[e] + (pairs of expert e before i). A "pair CTA" owns pairs [a, b): it counts every pair's
 // expert and those before a (one pass over the T * K expert ids, from L2), scans the counts into
-// offsets, ranks its own pairs in order, and writes each pair's position and its token's row split
-// exactly into e4m3 hi + lo rows (x * 2^e, e from the token's absolute maximum). "Shared CTAs"
-// write the shared expert's positions P + t. CTA 0 also writes the tile list (ceil(n_e / 64) tiles
+// offsets, ranks its own pairs in order, and writes each pair's position and copies its token's
+// hi + lo rows (the exact e4m3 split of x * 2^e, e from the token's absolute maximum, made once per
+// token by the select kernel) to it. "Shared CTAs" write the shared expert's positions P + t. CTA 0 also writes the tile list (ceil(n_e / 64) tiles
 // per expert in expert order, then the shared expert's tiles), the per-expert offsets and the
 // counts the expert kernels read.
 constexpr int kDispThreads = 256;
@@ -1356,9 +1381,24 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
     const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.out_bias + n)), b1 = __ldg(reinterpret_cast<const float4*>(p.out_bias + n + 4));
     bias[0] = b0.x, bias[1] = b0.y, bias[2] = b0.z, bias[3] = b0.w, bias[4] = b1.x, bias[5] = b1.y, bias[6] = b1.z, bias[7] = b1.w;
   }
+  const bool ep = p.world > 1;
+  const int K = p.K;
+  // the pairs' positions and weights (dispatch and select, which completed before the up kernel
+  // started) and the shared gate are read before the wait; only the rows come from the down kernel
+  int pos[kMaxTopK];
+  float w[kMaxTopK];
+  float gate = 0.f;
+  if (active) {
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      // expert parallel: pair t * K + j's row is row t * K + j of the return buffer
+      pos[j] = j < K ? (ep ? t * K + j : __ldcg(ws_at<const int>(p, L.inv) + t * K + j)) : -1;
+      w[j] = j < K ? __ldcg(ws_at<const float>(p, L.pair_w) + t * K + j) : 0.f;
+    }
+    if (p.sh_w13 != nullptr) gate = __ldcg(ws_at<const float>(p, L.gate) + t);
+  }
   griddep_wait();
   griddep_launch();
-  const bool ep = p.world > 1;
   const EpLayout A = ep_layout(ep ? p.world : 1, p.ep_tl, p.K, p.H);
   if (ep) {
     // every destination rank has written this rank's output rows (bounded wait on its flag; a wait
@@ -1370,15 +1410,6 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
     __syncthreads();
   }
   if (!active) return;
-  const int K = p.K;
-  int pos[kMaxTopK];
-  float w[kMaxTopK];
-#pragma unroll
-  for (int j = 0; j < kMaxTopK; ++j) {
-    // expert parallel: pair t * K + j's row is row t * K + j of the return buffer
-    pos[j] = j < K ? (ep ? t * K + j : __ldcg(ws_at<const int>(p, L.inv) + t * K + j)) : -1;
-    w[j] = j < K ? __ldcg(ws_at<const float>(p, L.pair_w) + t * K + j) : 0.f;
-  }
   const float* outp = ws_at<const float>(p, L.outp);
   const float* rows = ep ? reinterpret_cast<const float*>(p.ep_arena[p.rank] + A.ret) : outp;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -1394,12 +1425,10 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const __grid_c
   }
   const bool sh = p.sh_w13 != nullptr;
   float shv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  float gate = 0.f;
   if (sh) {
     const float4* row = reinterpret_cast<const float4*>(outp + static_cast<size_t>(L.cap + t) * p.H + n);
     const float4 o0 = __ldcg(row), o1 = __ldcg(row + 1);
     shv[0] = o0.x, shv[1] = o0.y, shv[2] = o0.z, shv[3] = o0.w, shv[4] = o1.x, shv[5] = o1.y, shv[6] = o1.z, shv[7] = o1.w;
-    gate = __ldcg(ws_at<const float>(p, L.gate) + t);
   }
   __align__(16) __nv_bfloat16 out[8];
 #pragma unroll
