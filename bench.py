@@ -39,6 +39,7 @@ H, I, E, TOPK, T = 2048, 512, 256, 8, 2
 EXPERT_BYTES = 2 * I * H + H * I + (2 * I // 128) * (H // 128) * 4 + (H // 128) * (I // 128) * 4  # 3,146,496
 METRIC = "MoE decode layer throughput (2-row frame x layer / s); us/layer = 1e6 / (value / n_gpus)"
 PF_T = 512
+SPEAKER_FRAMES = 300  # the distilled-speaker workload: consecutive frames, each with its own rows
 PF_METRIC = "prefill MoE layer throughput (tokens / s), T=512 prompt rows, Zipf(1.1)-skewed routing"
 
 
@@ -395,14 +396,24 @@ def run_decode(args, world, rank, local, speaker=False):
     n_layers = args.layers
     kw = dict(experts=32, router_dtype=torch.float32, shared=True, bias=True) if speaker else {}
     layers = [make_layer(1000 * (rank + 1) + l, dev, **kw) for l in range(n_layers)]
+    # every layer's 2 rows of a frame live in xs_in [layers, T, H]; the speaker workload times
+    # SPEAKER_FRAMES consecutive frames, each with its own seeded rows, copied into xs_in before
+    # the frame's graph replay; the 256-expert decode replays one frame's rows
+    if speaker:
+        gx = torch.Generator(device=dev).manual_seed(4242 + rank)
+        xs_frames = rms(torch.randn(SPEAKER_FRAMES, n_layers, T, H, generator=gx, device=dev)).to(torch.bfloat16)
+        xs_in = xs_frames[0].clone()
+    else:
+        xs_frames = None
+        xs_in = torch.stack([L["x"] for L in layers])
     torch.cuda.synchronize()
     logits_bf16 = not speaker
-    outs = [layer_call(L, L["x"], logits_bf16) for L in layers]  # eager warm-up (creates the workspace)
+    outs = [layer_call(L, xs_in[l], logits_bf16) for l, L in enumerate(layers)]  # eager warm-up (workspace)
     torch.cuda.synchronize()
     bytes_step = sum(layer_bytes(L, o[1]) for L, o in zip(layers, outs))
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        gouts = [layer_call(L, L["x"], logits_bf16) for L in layers]
+        gouts = [layer_call(L, xs_in[l], logits_bf16) for l, L in enumerate(layers)]
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -414,28 +425,32 @@ def run_decode(args, world, rank, local, speaker=False):
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = SPEAKER_FRAMES if speaker else args.steps
     with ClockSampler(local) as clk:
         e0.record()
-        for _ in range(args.steps):
+        for f in range(steps):
+            if speaker:
+                xs_in.copy_(xs_frames[f])  # the frame's rows (320 KB, device to device)
             graph.replay()
         e1.record()
         torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    # kernels per layer as the library reports them (route, up, down, combine)
-    launches = args.steps * n_layers * dm3._lib.load().dm3_last_launch_count()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    # kernels per layer as the library reports them (route, cluster, finish)
+    launches = steps * n_layers * dm3._lib.load().dm3_last_launch_count()
 
     # end to end through the public op with host buffers: every layer's rows H2D from pinned memory
     # (one copy), the captured frame, and the frame's result (the last layer's rows) D2H
-    xs_host = torch.stack([L["x"].cpu() for L in layers]).pin_memory()
+    xs_host_all = (xs_frames if speaker else xs_in.unsqueeze(0)).cpu().pin_memory()
+    xs_host = xs_host_all[0]
     y_host = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    xs_dev = torch.stack([L["x"] for L in layers])
+    xs_dev = xs_in.clone()
     g2 = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g2):
         g2outs = [layer_call(L, xs_dev[l], logits_bf16)[0] for l, L in enumerate(layers)]
 
-    def e2e_step():
-        xs_dev.copy_(xs_host, non_blocking=True)
+    def e2e_step(f=0):
+        xs_dev.copy_(xs_host_all[f % xs_host_all.shape[0]], non_blocking=True)
         g2.replay()
         y_host.copy_(g2outs[-1], non_blocking=True)
 
@@ -445,12 +460,12 @@ def run_decode(args, world, rank, local, speaker=False):
     barrier(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
-    for _ in range(args.steps):
-        e2e_step()
+    for f in range(steps):
+        e2e_step(f)
     f1.record()
     torch.cuda.synchronize()
     barrier(world)
-    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / args.steps, world)
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / steps, world)
 
     pk = peaks()
     achieved = bytes_step / (ms * 1e-3) / 1e9
@@ -460,7 +475,7 @@ def run_decode(args, world, rank, local, speaker=False):
         "value": round(value, 1),
         "unit": "layer-frames/s",
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "us_per_layer": round(ms * 1000.0 / n_layers, 3),
@@ -477,6 +492,8 @@ def run_decode(args, world, rank, local, speaker=False):
             "shared_expert": "block-FP8 128x128 + bf16 sigmoid gate",
             "scales": "128x128 fp32", "cuda_graph": True,
             "l2": "no flush: 40 layers stream > 2 GB of weights per step (L2 126 MB)",
+            "frames": (f"{SPEAKER_FRAMES} consecutive frames, each with its own seeded rows per layer (one step = one "
+                       "frame)" if speaker else "one frame's rows replayed (one step = one frame of 40 layers)"),
             "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
         },
         "roofline": {
@@ -486,7 +503,7 @@ def run_decode(args, world, rank, local, speaker=False):
             "unit": "GB/s",
             "frac": round(achieved / pk["hbm_gbs"], 4),
             "peak_source": f"{pk['source']} HBM copy bandwidth",
-            "kernel": ("one decode layer: dm3::moe route_kernel + layer_kernel (2-CTA clusters)"
+            "kernel": ("one decode layer: dm3::moe route_kernel + layer_kernel (2-CTA clusters) + finish_kernel"
                        if os.environ.get("DM3_CLUSTER", "1") != "0"
                        else "one decode layer: dm3::moe route + up + down + combine kernels"),
             "bytes_per_launch": round(bytes_step / n_layers),
