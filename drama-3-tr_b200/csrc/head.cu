@@ -60,8 +60,10 @@ __global__ void __launch_bounds__(kThreads) finish_kernel(const __grid_constant_
   __shared__ int s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c0 = blockIdx.x * kColsPerCta;
-  griddep_wait();
+  // the dependents (direction_score, then the next frame's GEMV, whose weight copies need no input)
+  // may start now; each waits for its own predecessor before reading
   griddep_launch();
+  griddep_wait();
   const float st = __ldg(p.strength);
   float l[2][kColsPerThread];
   float m[2] = {-INFINITY, -INFINITY}, s[2] = {0.f, 0.f};
@@ -140,8 +142,8 @@ __global__ void __launch_bounds__(kThreads) finish_kernel(const __grid_constant_
 // token - semantic_begin + 1 (direction_score, engine.py:476-479).
 __global__ void score_kernel(const float* logits, const float* lse, int Nc, const int64_t* token, int64_t eos_id,
                              int64_t sem_begin, float* score) {
+  griddep_launch();  // as in finish_kernel: the next frame's GEMV may stage its weights meanwhile
   griddep_wait();
-  griddep_launch();
   if (threadIdx.x != 0) return;
   const int64_t t = *token;
   int64_t i = t == eos_id ? 0 : t - sem_begin + 1;

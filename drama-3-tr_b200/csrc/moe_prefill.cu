@@ -55,7 +55,10 @@ __host__ __device__ constexpr int epi_groups(bool down) { return down ? 1 : 2; }
 __host__ __device__ constexpr int expert_threads(bool down) { return 96 + epi_groups(down) * kEpiThreads; }
 constexpr int kStages = 4;                   // ring of TMA stages
 constexpr int kStage = 3 * kSlab;            // two weight slabs, the activation slab (<= 128 rows)
-constexpr int kNacc = 2;                     // TMEM accumulator buffers of 256 columns
+// TMEM accumulator buffers: up 4 of 128 columns (gate, then up rows; a token's hi and lo rows add into
+// one column), down 2 of 256 (two 128-row halves, each token's hi / lo rows in adjacent columns)
+__host__ __device__ constexpr int n_acc(bool down) { return down ? 2 : 4; }
+__host__ __device__ constexpr uint32_t acc_cols(bool down) { return down ? 256u : 128u; }
 constexpr int kLgK = 512;                    // K per logits CTA
 constexpr int kLgSlabs = kLgK / 64;          // 64 bf16 per 128-byte slab
 constexpr int kLgTok = 32;                   // tokens per logits CTA (N)
@@ -160,7 +163,7 @@ __host__ __device__ inline Layout layout(int T, int H, int I, int E, int K, int 
   o += P * 4;
   L.tiles = o = aup(o, 128);
   o += static_cast<size_t>(L.max_tiles) * 16;
-  L.pimg = o = aup(o, 1024);  // [npos][2][H] e4m3: hi row, lo row
+  L.pimg = o = aup(o, 1024);  // [2][npos][H] e4m3: the hi rows of every position, then the lo rows
   o += static_cast<size_t>(L.npos) * 2 * H;
   L.himg = o = aup(o, 1024);  // [npos][2][I] e4m3
   o += static_cast<size_t>(L.npos) * 2 * I;
@@ -618,8 +621,8 @@ __device__ __forceinline__ void split_row(const Params& p, const Layout& L, int 
   const float sc = exp2i(ex);
   if (lane == 0) ws_at<float>(p, L.pxinv)[pos] = exp2i(-ex);
   const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
-  uint8_t* hi_row = p.ws + L.pimg + static_cast<size_t>(2 * pos) * p.H;
-  uint8_t* lo_row = hi_row + p.H;
+  uint8_t* hi_row = p.ws + L.pimg + static_cast<size_t>(pos) * p.H;
+  uint8_t* lo_row = p.ws + L.pimg + static_cast<size_t>(L.npos + pos) * p.H;
   constexpr int kC = kMaxH / 16 / 32;  // 16-element chunks per lane at H = 2048
   uint4 v[kC][2];
 #pragma unroll
@@ -655,18 +658,25 @@ struct RecvPairs {
   }
 };
 
-// Copies a received pair's hi / lo rows from the staging area into position pos (one warp).
+// Copies a received pair's hi / lo rows (adjacent in the staging area) into position pos of the hi
+// and lo planes (one warp).
 __device__ __forceinline__ void copy_row(const Params& p, const Layout& L, const uint8_t* srow, int pos, int lane) {
-  uint8_t* drow = p.ws + L.pimg + static_cast<size_t>(2 * pos) * p.H;
-  const int n16 = 2 * p.H / 16;
+  uint4* hi_row = reinterpret_cast<uint4*>(p.ws + L.pimg + static_cast<size_t>(pos) * p.H);
+  uint4* lo_row = reinterpret_cast<uint4*>(p.ws + L.pimg + static_cast<size_t>(L.npos + pos) * p.H);
+  const int h16 = p.H / 16, n16 = 2 * h16;
   constexpr int kC = 2 * kMaxH / 16 / 32;
   uint4 v[kC];
 #pragma unroll
   for (int i = 0; i < kC; ++i)
     if (lane + 32 * i < n16) v[i] = __ldcg(reinterpret_cast<const uint4*>(srow) + lane + 32 * i);
 #pragma unroll
-  for (int i = 0; i < kC; ++i)
-    if (lane + 32 * i < n16) reinterpret_cast<uint4*>(drow)[lane + 32 * i] = v[i];
+  for (int i = 0; i < kC; ++i) {
+    const int c = lane + 32 * i;
+    if (c < h16)
+      hi_row[c] = v[i];
+    else if (c < n16)
+      lo_row[c - h16] = v[i];
+  }
 }
 
 __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_constant__ Params p) {
@@ -963,8 +973,11 @@ struct Aux {
   float amax[2][2][2][4][32];  // up: [group][item parity][token half][lane quarter][token] |h| maxima
 };
 
-// Activation box of a tile of n tokens: 2n rows rounded up to 16, 32, 64 or 128 (the MMA's N).
+// Activation box of a tile of n tokens (index 0-3 for n <= 8, 16, 32, 64). Up: n rows of the hi
+// plane and n of the lo plane, each rounded up to 16, 16, 32 or 64 rows (the MMA's N; M = 128 needs a
+// multiple of 16). Down: the 2n interleaved hi / lo rows, rounded up to 16, 32, 64 or 128.
 __device__ __forceinline__ int box_index(int n) { return n <= 8 ? 0 : n <= 16 ? 1 : n <= 32 ? 2 : 3; }
+__host__ __device__ constexpr int up_box_rows(int bi) { return bi <= 1 ? 16 : (8 << bi); }
 
 // Item k of this CTA (k-th of blockIdx.x, blockIdx.x + gridDim.x, ...): staged in shared memory at
 // kernel start, read from the tile list beyond kMaxItems.
@@ -984,7 +997,8 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr int kBOff = 2 * kSlab;  // activation slab inside a stage
-  constexpr uint32_t kAccCols = 256;
+  constexpr int kNacc = n_acc(DOWN);
+  constexpr uint32_t kAccCols = acc_cols(DOWN);
   Aux& aux = *reinterpret_cast<Aux*>(smem + kStages * kStage);
   const Layout L = layout_of(p);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1038,7 +1052,8 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
         const int plane = it.x < 0 ? 0 : it.x;
         uint8_t* dst = smem + (s % kStages) * kStage;
         uint64_t* bar = &aux.full[s % kStages];
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kBOff + (16 << box_index(it.z)) * 128));
+        const int bi = box_index(it.z);
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(kBOff + (DOWN ? (16 << bi) : 2 * up_box_rows(bi)) * 128));
         const int row0 = DOWN ? 2 * kRows * it.w : kRows * it.w;
         const int row1 = DOWN ? row0 + kRows : p.I + kRows * it.w;
         tc::tma_load_3d(dst, map, kb * 128, row0, plane, bar);
@@ -1047,7 +1062,14 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
       auto issue_b = [&](int s, const int4& it, int kb) {
         const int bi = box_index(it.z);
         const CUtensorMap* map = bi == 0 ? &map_b0 : bi == 1 ? &map_b1 : bi == 2 ? &map_b2 : &map_b3;
-        tc::tma_load_3d(smem + (s % kStages) * kStage + kBOff, map, kb * 128, 2 * it.y, 0, &aux.full[s % kStages]);
+        uint8_t* dst = smem + (s % kStages) * kStage + kBOff;
+        if (DOWN) {
+          tc::tma_load_3d(dst, map, kb * 128, 2 * it.y, 0, &aux.full[s % kStages]);
+        } else {
+          // the tile's hi rows, then its lo rows, from the two planes of the activation image
+          tc::tma_load_3d(dst, map, kb * 128, it.y, 0, &aux.full[s % kStages]);
+          tc::tma_load_3d(dst + up_box_rows(bi) * 128, map, kb * 128, it.y, 1, &aux.full[s % kStages]);
+        }
       };
       // the weight slabs of the first ring before the wait; activation slabs (from the preceding
       // kernel) after it
@@ -1080,20 +1102,35 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
       int s = 0, use = 0;
       for (int k = 0; k < my_items; ++k) {
         const int4 it = item_desc(aux, tiles, nrb, k);
-        const uint32_t idesc = tc::idesc_e4m3(kRows, 16 << box_index(it.z));
+        const int bi = box_index(it.z);
+        const int nb = DOWN ? (16 << bi) : up_box_rows(bi);  // the MMA's N
+        const uint32_t idesc = tc::idesc_e4m3(kRows, nb);
         for (int kb = 0; kb < nkb; ++kb, ++s, ++use) {
           const int ab = use % kNacc;
-          if (ab != par) continue;
+          if ((ab & 1) != par) continue;
           wait_or_abort(p, &aux.acc_empty[ab], ((use / kNacc) & 1) ^ 1u, abort);
           wait_or_abort(p, &aux.full[s % kStages], (s / kStages) & 1, abort);
           tc::fence_after_sync();
           const uint32_t a = smem_u32(smem + (s % kStages) * kStage);
           const uint32_t b = a + kBOff;
           const uint32_t d = tmem + ab * kAccCols;
+          if (DOWN) {
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            tc::mma_f8(d, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
-            tc::mma_f8(d + 128, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+            for (int k4 = 0; k4 < 4; ++k4) {
+              tc::mma_f8(d, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+              tc::mma_f8(d + 128, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+            }
+          } else {
+            // x = hi + lo exactly: both halves of a token add into its column (gate rows in columns
+            // [0, 64), up rows in [64, 128))
+            const uint32_t blo = b + nb * 128;
+#pragma unroll
+            for (int k4 = 0; k4 < 4; ++k4) {
+              tc::mma_f8(d, tc::smem_desc(a + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+              tc::mma_f8(d, tc::smem_desc(a + 32 * k4), tc::smem_desc(blo + 32 * k4), idesc, true);
+              tc::mma_f8(d + 64, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(b + 32 * k4), idesc, k4 > 0);
+              tc::mma_f8(d + 64, tc::smem_desc(a + kSlab + 32 * k4), tc::smem_desc(blo + 32 * k4), idesc, true);
+            }
           }
           tc::mma_commit(&aux.empty[s % kStages]);
           tc::mma_commit(&aux.acc_full[ab]);
@@ -1199,24 +1236,26 @@ __global__ void __launch_bounds__(expert_threads(DOWN), 1)
           ++use;
           tc::fence_after_sync();
           if (nh > 0 && ready) {
-            const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + 64 * hf;
+            const uint32_t ta =
+                tmem + (static_cast<uint32_t>(32 * q) << 16) + ab * kAccCols + (DOWN ? 64 : 32) * hf;
             if (!DOWN) {
-              // 16 columns (8 tokens' hi / lo) per load keep the two groups within 112 registers
+              // the thread's 32 tokens: one column each (hi + lo summed by the MMAs), gate rows, then up
+              // rows; 16 columns per load keep the two groups within their registers
 #pragma unroll
-              for (int c = 0; c < 4; ++c) {
+              for (int c = 0; c < 2; ++c) {
                 float v[16];
                 tc::tmem_ld16(ta + 16 * c, v);
                 tc::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 8; ++j) a0[8 * c + j] = fmaf(sg, v[2 * j] + v[2 * j + 1], a0[8 * c + j]);
+                for (int j = 0; j < 16; ++j) a0[16 * c + j] = fmaf(sg, v[j], a0[16 * c + j]);
               }
 #pragma unroll
-              for (int c = 0; c < 4; ++c) {
+              for (int c = 0; c < 2; ++c) {
                 float v[16];
-                tc::tmem_ld16(ta + 128 + 16 * c, v);
+                tc::tmem_ld16(ta + 64 + 16 * c, v);
                 tc::tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 8; ++j) a1[8 * c + j] = fmaf(su, v[2 * j] + v[2 * j + 1], a1[8 * c + j]);
+                for (int j = 0; j < 16; ++j) a1[16 * c + j] = fmaf(su, v[j], a1[16 * c + j]);
               }
             } else {
               float v0[32], v1[32];
@@ -1512,7 +1551,9 @@ int launch_prefill(const pf::Params& p, cudaStream_t stream, int phases = 3) {
     msh2 = m2;
   }
   for (int b = 0; b < 4 && (phases & 2); ++b) {
-    ok = ok && tensor_map_3d(&mb_up[b], p.ws + L.pimg, H, rows2, 1, H, rows2 * H, 16u << b);
+    // up: the hi plane (d2 = 0) and the lo plane (d2 = 1) of [2][npos][H]
+    ok = ok && tensor_map_3d(&mb_up[b], p.ws + L.pimg, H, L.npos, 2, H, static_cast<uint64_t>(L.npos) * H,
+                             static_cast<uint32_t>(pf::up_box_rows(b)));
     ok = ok && tensor_map_3d(&mb_dn[b], p.ws + L.himg, I, rows2, 1, I, rows2 * I, 16u << b);
   }
   if (!ok) return 2;
