@@ -19,8 +19,10 @@ __host__ __device__ inline size_t aup(size_t v, size_t a) { return (v + a - 1) /
 //            rank have landed in stage[s] (count first, then the epoch with a system-scope release)
 //   retflag  [world] u32: written by destination rank d after every output row for this rank's
 //            pairs has landed in ret
-//   rmeta    [world][tl * K] int2: (local expert << 20 | source pair index, x split exponent)
-//   stage    [world][tl * K][2][H] e4m3: the pairs' x rows, split exactly into hi + lo
+//   rmeta    [world][tl * K] int2: (local expert << 20 | source pair index,
+//            the token's row slot in stage << 9 | x split exponent + 256)
+//   stage    [world][tl * K][2][H] e4m3: the x rows (one per token and destination rank, numbered
+//            in pair order), split exactly into hi + lo
 //   ret      [tl * K][H] fp32: the down-projection row of each of this rank's pairs
 //   redflag  [world] u32, red [2][world][2][kMaxT][H] fp32: the sharded decode layer's
 //            all-reduce, rank s's routed and shared partial sums (written by s; the region of the

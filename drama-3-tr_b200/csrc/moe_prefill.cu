@@ -850,11 +850,12 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_con
       int src, slot;
       rp.locate(a + j, p.world, src, slot);
       const int2 m = __ldcg(&rmeta[src * A.slots + slot]);
+      const int row = m.y >> 9, ex = (m.y & 0x1FF) - 256;  // the pair's token row, its split exponent
       if (lane == 0) {
-        ws_at<float>(p, L.pxinv)[pos] = exp2i(-m.y);
+        ws_at<float>(p, L.pxinv)[pos] = exp2i(-ex);
         ws_at<int>(p, L.pos_tok)[pos] = (src << 20) | (m.x & 0xFFFFF);  // where the output row goes
       }
-      copy_row(p, L, arena + A.stage + (static_cast<size_t>(src) * A.slots + slot) * 2 * p.H, pos, lane);
+      copy_row(p, L, arena + A.stage + (static_cast<size_t>(src) * A.slots + row) * 2 * p.H, pos, lane);
     }
   }
 }
@@ -867,8 +868,8 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_kernel(const __grid_con
 // a local counter after a system-scope fence by each CTA) writes every destination's count and then
 // its flag (the call's epoch, with a system-scope release), and advances the local epoch.
 __global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_constant__ Params p) {
-  __shared__ int dcount[kMaxRanks], dbefore[kMaxRanks];
-  __shared__ int spos[kMaxPpc];
+  __shared__ int dcount[kMaxRanks], dbefore[kMaxRanks], rbefore[kMaxRanks];
+  __shared__ int spos[kMaxPpc], srow[kMaxPpc];
   __shared__ int s_last;
   const Layout L = layout_of(p);
   const EpLayout A = ep_layout(p.world, p.ep_tl, p.K, p.H);
@@ -883,39 +884,101 @@ __global__ void __launch_bounds__(kDispThreads) ep_dispatch_kernel(const __grid_
   if (tid < kMaxRanks) {
     dcount[tid] = 0;
     dbefore[tid] = 0;
+    rbefore[tid] = 0;
   }
   __syncthreads();
   const int* pair_e = ws_at<const int>(p, L.pair_e);
-  for (int i = tid; i < P; i += kDispThreads) {
-    const int d = ep_place(p, __ldcg(pair_e + i)) >> 16;
-    atomicAdd(&dcount[d], 1);
-    if (i < a) atomicAdd(&dbefore[d], 1);
+  // A token's row goes to a destination once, with its first pair (in k order) to that rank; the
+  // token's other pairs there point at that row. Rows are numbered per destination in pair order.
+  // (When K does not divide a CTA's pair range or a 32-lane round, every pair carries its own row.)
+  const bool share = (ppc % K) == 0 && (32 % K) == 0;
+  auto dest = [&](int i) { return ep_place(p, __ldcg(pair_e + i)) >> 16; };
+  if (share) {
+    // one token per thread: its pairs' ranks, and which pair is the first to each rank
+    for (int t = tid; t < p.T; t += kDispThreads) {
+      int dk[kMaxTopK];
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k) dk[k] = k < K ? dest(t * K + k) : -1;
+#pragma unroll
+      for (int k = 0; k < kMaxTopK; ++k) {
+        if (k >= K) break;
+        const int d = dk[k];
+        atomicAdd(&dcount[d], 1);
+        if (t * K + k < a) {
+          atomicAdd(&dbefore[d], 1);
+          bool first = true;
+#pragma unroll
+          for (int k2 = 0; k2 < kMaxTopK; ++k2)
+            if (k2 < k && dk[k2] == d) first = false;
+          if (first) atomicAdd(&rbefore[d], 1);
+        }
+      }
+    }
+  } else {
+    for (int i = tid; i < P; i += kDispThreads) {
+      const int d = dest(i);
+      atomicAdd(&dcount[d], 1);
+      if (i < a) {
+        atomicAdd(&dbefore[d], 1);
+        atomicAdd(&rbefore[d], 1);
+      }
+    }
   }
   __syncthreads();
   if (warp == 0) {
+    // pair slots and row slots of this CTA's pairs, in pair order (when rows are shared, a token's K
+    // pairs lie in one 32-lane round)
     for (int i0 = a; i0 < b; i0 += 32) {
       const int i = i0 + lane;
-      const int d = i < b ? ep_place(p, __ldcg(pair_e + i)) >> 16 : -1;
+      const int d = i < b ? dest(i) : -1;
       const unsigned m = __match_any_sync(0xffffffffu, d);
       const int rank = d >= 0 ? dbefore[d] + __popc(m & ((1u << lane) - 1u)) : 0;
+      bool owner = d >= 0;
+      if (share) {
+        const int k = i % K;
+        for (int j = 1; j < kMaxTopK; ++j) {
+          const int dj = __shfl_sync(0xffffffffu, d, lane >= j ? lane - j : lane);
+          if (j <= k && dj == d) owner = false;
+        }
+      }
+      const unsigned mo = m & __ballot_sync(0xffffffffu, owner);
+      int row = d >= 0 ? rbefore[d] + __popc(mo & ((1u << lane) - 1u)) : 0;
+      // a shared row's slot is that of the token's first pair to the same rank
+      const unsigned mt = __match_any_sync(0xffffffffu, share ? (i / K) * kMaxRanks + (d < 0 ? 0 : d) : i);
+      const int row_owner = __ffs(mt & __ballot_sync(0xffffffffu, owner)) - 1;
+      const int shared_row = __shfl_sync(0xffffffffu, row, row_owner < 0 ? lane : row_owner);
+      if (!owner) row = shared_row;
       __syncwarp();
-      if (d >= 0 && lane == __ffs(m) - 1) dbefore[d] += __popc(m);
+      if (d >= 0 && lane == __ffs(m) - 1) {
+        dbefore[d] += __popc(m);
+        rbefore[d] += __popc(mo);
+      }
       __syncwarp();
-      if (i < b) spos[i - a] = (d << 24) | rank;
+      if (i < b) {
+        spos[i - a] = (d << 24) | rank;
+        srow[i - a] = owner ? row : -1 - row;
+      }
     }
   }
   __syncthreads();
   for (int j = warp; j < b - a; j += kDispWarps) {
     const int i = a + j, t = i / K;
     const int d = spos[j] >> 24, slot = spos[j] & 0xFFFFFF;
+    const bool owner = srow[j] >= 0;
+    const int row = owner ? srow[j] : -1 - srow[j];
     const int e_local = ep_place(p, __ldcg(pair_e + i)) & 0xFFFF;
     uint8_t* dst_arena = p.ep_arena[d];
     const size_t sidx = static_cast<size_t>(p.rank) * A.slots + slot;
+    const size_t ridx = static_cast<size_t>(p.rank) * A.slots + row;
     const int ex = __ldcg(ws_at<const int>(p, L.xexp) + t);
-    if (lane == 0) reinterpret_cast<int2*>(dst_arena + A.rmeta)[sidx] = make_int2((e_local << 20) | i, ex);
+    // metadata: (local expert, pair index), (the token's row slot, split exponent + 256 in 9 bits)
+    if (lane == 0)
+      reinterpret_cast<int2*>(dst_arena + A.rmeta)[sidx] =
+          make_int2((e_local << 20) | i, (row << 9) | ((ex + 256) & 0x1FF));
+    if (!owner) continue;  // the token's row already goes to this rank with an earlier pair
     const float sc = exp2i(ex);
     const uint4* src = reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(t) * p.H);
-    uint8_t* hi_row = dst_arena + A.stage + sidx * 2 * p.H;
+    uint8_t* hi_row = dst_arena + A.stage + ridx * 2 * p.H;
     uint8_t* lo_row = hi_row + p.H;
     constexpr int kC = kMaxH / 16 / 32;
     uint4 v[kC][2];
