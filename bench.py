@@ -236,6 +236,19 @@ def check_decode_sharded(grp, world, rank, dev) -> dict:
             "rel_l2": [round(e, 7) for e in errs]}
 
 
+def observed_placement(gate, logit_bias, world: int, dev, seed: int):
+    """Expert placement from observed loads, as a deployment would calibrate it: route a seeded
+    calibration batch of PF_T rows (not the measured rows) through the layer's router once and balance
+    the per-expert pair counts over the ranks (greedy LPT, equal experts per rank)."""
+    import drama3_b200 as dm3
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    calib = rms(torch.randn(PF_T, H, generator=g, device=dev)).to(torch.bfloat16)
+    ids, _ = dm3.ops.route(calib, gate, TOPK, True, logit_bias)
+    counts = torch.bincount(ids.flatten(), minlength=E).double().cpu()
+    return dm3.ep.balanced_placement(counts + 1e-3, world)
+
+
 def check_prefill_ep(grp, world, rank, dev, placement) -> dict:
     """The expert-parallel prefill against the one-GPU prefill of all 512 tokens on this rank's GPU,
     the same seeded full layer on every rank: this rank's outputs, ids and weights bit-identical,
@@ -246,8 +259,9 @@ def check_prefill_ep(grp, world, rank, dev, placement) -> dict:
     ref = prefill_call(L, L["x"])
     tl = PF_T // world
     owner = None
-    if placement == "balanced":
-        owner = dm3.ep.balanced_placement(torch.exp(L["logit_bias"].float().cpu()), world)
+    if placement in ("balanced", "observed"):
+        owner = (observed_placement(L["gate"], L["logit_bias"], world, dev, 4322 + 13) if placement == "observed"
+                 else dm3.ep.balanced_placement(torch.exp(L["logit_bias"].float().cpu()), world))
         mine = dm3.ep.local_experts(owner, rank).to(dev)
         owner = owner.to(dev)
     else:
@@ -557,8 +571,9 @@ def prefill_bytes(L, ids: torch.Tensor) -> int:
 
 
 def run_prefill_ep(args, world, rank, local):
-    """Expert parallel over `world` GPUs: T=512 tokens in total (512 / world per rank), rank r owns
-    experts [r * 256 / world, (r + 1) * 256 / world); NVLink dispatch / return inside the kernels."""
+    """Expert parallel over `world` GPUs: T=512 tokens in total (512 / world per rank), 256 / world
+    experts per rank placed by --ep-placement (default: balanced on observed loads); NVLink dispatch /
+    return inside the kernels."""
     import drama3_b200 as dm3
 
     dev = torch.device("cuda", local)
@@ -579,8 +594,14 @@ def run_prefill_ep(args, world, rank, local):
         gb = torch.Generator(device="cpu").manual_seed(seed + 7)
         bias_cpu = -1.1 * torch.log(torch.randperm(E, generator=gb).float() + 1.0)
         L["logit_bias"] = bias_cpu.to(dev)
-        # expected expert load follows exp(bias) = rank^-1.1; the balanced placement evens it out
-        L["owner"] = dm3.ep.balanced_placement(torch.exp(bias_cpu), world).to(dev) if placement == "balanced" else None
+        # observed: balance the pair counts of a calibration batch; balanced: the expected load
+        # exp(bias) = rank^-1.1 (which ignores that a token's top-8 are distinct experts)
+        if placement == "observed":
+            L["owner"] = observed_placement(L["gate"], L["logit_bias"], world, dev, seed + 13).to(dev)
+        elif placement == "balanced":
+            L["owner"] = dm3.ep.balanced_placement(torch.exp(bias_cpu), world).to(dev)
+        else:
+            L["owner"] = None
         gx = torch.Generator(device=dev).manual_seed(seed + 11)
         x = rms(torch.randn(PF_T, H, generator=gx, device=dev)).to(torch.bfloat16)
         L["x"] = x[rank * tl:(rank + 1) * tl].contiguous()
@@ -683,8 +704,10 @@ def run_prefill_ep(args, world, rank, local):
             "experts": E, "top_k": TOPK, "router": "bf16, logits rounded to bf16, + Zipf bias",
             "shared_expert": "block-FP8 128x128 + bf16 sigmoid gate (on each token's home rank)",
             "parallelism": f"expert parallel x{world}: {el} experts and {tl} tokens per rank, NVLink peer stores",
-            "placement": placement + (" (greedy LPT on the expected load exp(bias))" if placement == "balanced"
-                                      else " blocks of 256 / n_gpus experts"),
+            "placement": placement + {"observed": " (greedy LPT on the pair counts of a separate seeded calibration "
+                                                  "batch routed once)",
+                                      "balanced": " (greedy LPT on the expected load exp(bias))",
+                                      "contiguous": " (blocks of 256 / n_gpus experts)"}[placement],
             "pairs_received_per_rank": recv, "cuda_graph": True,
         },
         "roofline": {
@@ -1118,7 +1141,7 @@ def main():
                     help="default workload: skip the prefill / GEMV objects (N=1) or the NVLink objects (N>1)")
     ap.add_argument("--decode-mode", default="replicas", choices=["replicas", "sharded"],
                     help="n_gpus > 1 decode: independent replicas (weak scaling) or one frame sharded (strong)")
-    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
+    ap.add_argument("--ep-placement", default="observed", choices=["observed", "balanced", "contiguous"],
                     help="expert placement of the expert-parallel prefill (n_gpus > 1)")
     args = ap.parse_args()
     world, rank, local = dist_setup()
