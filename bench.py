@@ -239,14 +239,16 @@ def check_decode_sharded(grp, world, rank, dev) -> dict:
 def observed_placement(gate, logit_bias, world: int, dev, seed: int):
     """Expert placement from observed loads, as a deployment would calibrate it: route a seeded
     calibration batch of PF_T rows (not the measured rows) through the layer's router once and balance
-    the per-expert pair counts over the ranks (greedy LPT, equal experts per rank)."""
+    the experts' 64-token tiles over the ranks (greedy LPT, equal experts per rank): an expert kernel's
+    time follows its tiles, each a fixed amount of weight streaming, more than its pairs."""
     import drama3_b200 as dm3
 
     g = torch.Generator(device=dev).manual_seed(seed)
     calib = rms(torch.randn(PF_T, H, generator=g, device=dev)).to(torch.bfloat16)
     ids, _ = dm3.ops.route(calib, gate, TOPK, True, logit_bias)
     counts = torch.bincount(ids.flatten(), minlength=E).double().cpu()
-    return dm3.ep.balanced_placement(counts + 1e-3, world)
+    tiles = torch.ceil(counts / 64.0)
+    return dm3.ep.balanced_placement(tiles + counts * 1e-4 + 1e-6, world)
 
 
 def check_prefill_ep(grp, world, rank, dev, placement) -> dict:
