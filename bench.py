@@ -246,9 +246,7 @@ def observed_placement(gate, logit_bias, world: int, dev, seed: int):
     g = torch.Generator(device=dev).manual_seed(seed)
     calib = rms(torch.randn(PF_T, H, generator=g, device=dev)).to(torch.bfloat16)
     ids, _ = dm3.ops.route(calib, gate, TOPK, True, logit_bias)
-    counts = torch.bincount(ids.flatten(), minlength=E).double().cpu()
-    tiles = torch.ceil(counts / 64.0)
-    return dm3.ep.balanced_placement(tiles + counts * 1e-4 + 1e-6, world)
+    return dm3.ep.tile_balanced_placement(torch.bincount(ids.flatten(), minlength=E), world)
 
 
 def check_prefill_ep(grp, world, rank, dev, placement) -> dict:

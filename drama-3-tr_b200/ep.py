@@ -2,7 +2,8 @@
 
 The reference spreads a prompt's tokens over the experts with ids.unique() / slot_map on one
 device (OnDemandExperts.forward, engine.py:138-147). Here each of `world` ranks owns
-E / world experts (rank r: [r * E / world, (r + 1) * E / world)) and routes its own share of the
+E / world experts (contiguous blocks, or as a placement table assigns them: `balanced_placement`
+on expected loads, `tile_balanced_placement` on observed ones) and routes its own share of the
 tokens. The kernels write every (token, k) pair's rows straight into the owning rank's arena and
 every output row straight back into the source rank's arena over NVLink, with per-call epoch
 flags; there is no host synchronisation, so a call can be captured into a CUDA graph (every rank
@@ -54,6 +55,17 @@ def balanced_placement(load: Tensor, world: int) -> Tensor:
         for i, e in enumerate(sorted(members[r])):
             owner[e] = (r << 16) | i
     return owner
+
+
+def tile_balanced_placement(counts: Tensor, world: int, tile_tokens: int = 64) -> Tensor:
+    """A placement from observed routing: `counts` [E] are the (token, k) pairs each expert received
+    over a calibration batch. Balances the experts' tiles of `tile_tokens` tokens rather than their
+    pairs: the expert kernels stream each tile's weights once, so a rank's time follows its tiles (a
+    cold expert with 3 tokens costs a whole tile). Same return value as `balanced_placement`."""
+    c = counts.double().cpu()
+    tiles = torch.ceil(c / float(tile_tokens))
+    # pairs break ties between experts of equal tiles; the floor spreads unused experts evenly
+    return balanced_placement(tiles + c * 1e-4 + 1e-6, world)
 
 
 def local_experts(owner: Tensor, rank: int) -> Tensor:

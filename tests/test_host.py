@@ -1,5 +1,6 @@
 """Host-side logic on CPU: the drop-in quantisers (bit-exact to the oracle, which is pinned to the
-reference), scale-layout inference, FP8Linear/convert bookkeeping and shared-expert packing."""
+reference), scale-layout inference, FP8Linear/convert bookkeeping, shared-expert packing and the
+expert-parallel placement helpers."""
 
 import torch
 
@@ -68,3 +69,22 @@ def test_fake_impls_trace_on_meta(dm3):
     g = torch.empty(32, 2048, device="meta")
     y, ids, w = torch.ops.dm3.moe_layer(x, g, 8, False, None, w13, s13, w2, s2, None, None, None, None, None, None)
     assert y.shape == (2, 2048) and ids.shape == (2, 8) and ids.dtype == torch.int64 and w.dtype == torch.bfloat16
+
+
+def test_tile_balanced_placement(dm3):
+    """A placement from observed counts: every rank holds E / world experts with local indices
+    0 .. E / world - 1, and the ranks' tile totals differ by at most the largest expert's tiles
+    (greedy longest-processing-time on tiles of 64 tokens)."""
+    E, world = 256, 4
+    r = torch.arange(1, E + 1, dtype=torch.float64)
+    counts = torch.floor(4096 * r.pow(-1.1) / r.pow(-1.1).sum()).long()  # Zipf-skewed pair counts
+    counts = counts[torch.randperm(E, generator=torch.Generator().manual_seed(3))]
+    owner = dm3.ep.tile_balanced_placement(counts, world)
+    o = owner.long()
+    assert all(int(((o >> 16) == k).sum()) == E // world for k in range(world))
+    for k in range(world):
+        mine = dm3.ep.local_experts(owner, k)
+        assert sorted((o[mine] & 0xFFFF).tolist()) == list(range(E // world))
+    tiles = torch.ceil(counts.double() / 64)
+    per = [float(tiles[(o >> 16) == k].sum()) for k in range(world)]
+    assert max(per) - min(per) <= float(tiles.max())
