@@ -112,9 +112,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 // Orders prior generic-proxy accesses (seen through an acquire) before later async-proxy reads.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
-__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 
 // ---------------------------------------------------------------- gpu-scope flags
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
@@ -168,47 +165,6 @@ __device__ __forceinline__ void mma_e4m3(float (&d)[4], uint32_t a0, uint32_t a1
 }
 
 __device__ __forceinline__ uint4 ld_smem16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-
-// Raw products of a 16-row e4m3 tile (smem rows row_lo = tile row g, row_hi = g + 8) and the 8
-// split-activation B columns (bcol = column g) over the 128-wide k blocks kbs[0..NK): out[i][.] is
-// the fp32 partial of k block kbs[i] (C fragment layout). Every fragment is loaded before the first
-// MMA and each 32-wide k step has its own accumulator, so the loads and the 4 * NK MMAs overlap.
-// Each lane reads 16 contiguous bytes of its rows and its B column per 64 k, which fixes the same
-// k <-> fragment-slot permutation for A and B.
-template <int NK>
-__device__ __forceinline__ void tile_kblocks(float (&out)[NK][4], const uint8_t* row_lo, const uint8_t* row_hi,
-                                             const uint8_t* bcol, bool lo_ok, bool hi_ok, bool bvalid,
-                                             const int (&kbs)[NK], int q) {
-  uint4 a[NK][2], c[NK][2], b[NK][2];
-  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-  for (int i = 0; i < NK; ++i)
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int off = kbs[i] * 128 + 64 * j + 16 * q;
-      a[i][j] = lo_ok ? ld_smem16(row_lo + off) : z;
-      c[i][j] = hi_ok ? ld_smem16(row_hi + off) : z;
-      b[i][j] = bvalid ? ld_smem16(bcol + off) : z;
-    }
-  float t[NK][4][4];
-#pragma unroll
-  for (int i = 0; i < NK; ++i)
-#pragma unroll
-    for (int h = 0; h < 4; ++h)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) t[i][h][e] = 0.f;
-#pragma unroll
-  for (int i = 0; i < NK; ++i)
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      mma_e4m3(t[i][2 * j], a[i][j].x, c[i][j].x, a[i][j].y, c[i][j].y, b[i][j].x, b[i][j].y);
-      mma_e4m3(t[i][2 * j + 1], a[i][j].z, c[i][j].z, a[i][j].w, c[i][j].w, b[i][j].z, b[i][j].w);
-    }
-#pragma unroll
-  for (int i = 0; i < NK; ++i)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) out[i][e] = (t[i][0][e] + t[i][1][e]) + (t[i][2][e] + t[i][3][e]);
-}
 
 // ---------------------------------------------------------------- exact bf16 -> e4m3 hi/lo split
 // Power-of-two prescale 2^e that maps amax into [128, 256): every bf16 value v with
