@@ -148,7 +148,9 @@ __global__ void __launch_bounds__(kThreads, NCH <= 2 ? 2 : 1) gemv_kernel(const 
         }
       }
 #pragma unroll
-    for (int c = 0; c < NCH; ++c)
+    for (int c = 0; c < NCH; ++c) {
+      uint32_t hi[2][4], lo[2][4];
+      float inv[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int kb = c * 16 + 2 * warp + i;
@@ -184,41 +186,119 @@ __global__ void __launch_bounds__(kThreads, NCH <= 2 ? 2 : 1) gemv_kernel(const 
         if (two) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 8));
         const int ex = split_exponent(amax);
         const float pre = exp2i(ex);
-        uint32_t hi[4], lo[4];
+        inv[i] = exp2i(-ex);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           uint16_t h0, l0, h1, l1;
           split2(v[4 * e] * pre, v[4 * e + 1] * pre, h0, l0);
           split2(v[4 * e + 2] * pre, v[4 * e + 3] * pre, h1, l1);
-          hi[e] = h0 | (static_cast<uint32_t>(h1) << 16);
-          lo[e] = l0 | (static_cast<uint32_t>(l1) << 16);
+          hi[i][e] = h0 | (static_cast<uint32_t>(h1) << 16);
+          lo[i][e] = l0 | (static_cast<uint32_t>(l1) << 16);
         }
-        // columns: m = hi of x row m, 4 + m = lo; rows 2-3 stay zero when M <= 2
-        __syncwarp();
-        if (two) {
-          *reinterpret_cast<uint2*>(xw + m * 128 + c0) = make_uint2(hi[0], hi[1]);
-          *reinterpret_cast<uint2*>(xw + (4 + m) * 128 + c0) = make_uint2(lo[0], lo[1]);
-          *reinterpret_cast<uint2*>(xw + (2 + m) * 128 + c0) = make_uint2(0u, 0u);
-          *reinterpret_cast<uint2*>(xw + (6 + m) * 128 + c0) = make_uint2(0u, 0u);
-        } else {
-          *reinterpret_cast<uint4*>(xw + m * 128 + c0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          *reinterpret_cast<uint4*>(xw + (4 + m) * 128 + c0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        }
-        // inverse prescales of x rows 0-3 from the lanes that computed them
-        const float inv = exp2i(-ex);
-        const int src0 = (2 * (q & 1)) << (two ? 4 : 3), src1 = (2 * (q & 1) + 1) << (two ? 4 : 3);
-        const float i0 = __shfl_sync(0xffffffffu, inv, src0 & 31);
-        const float i1 = __shfl_sync(0xffffffffu, inv, src1 & 31);
-        ef[c][i][0] = (two && (q & 1)) ? 0.f : i0;
-        ef[c][i][1] = (two && (q & 1)) ? 0.f : i1;
-        __syncwarp();
-        bfr[c][i][0] = ld_smem16(xw + g * 128 + 16 * q);
-        bfr[c][i][1] = ld_smem16(xw + g * 128 + 64 + 16 * q);
       }
+      // B fragment columns: m = hi of x row m, 4 + m = lo. With M <= 2 both K blocks share the
+      // buffer: block i's hi and lo of x row m go to rows 2i + m and 4 + 2i + m, and lane group g
+      // reads row g ^ 2i, so that columns 0, 1, 4, 5 of block i's fragment hold its x rows 0, 1. Its
+      // columns 2, 3, 6, 7 then hold the other block's values: they meet zero prescale factors and
+      // land in partial sums of x rows 2, 3, which are never read. With M > 2 the blocks take the
+      // buffer in turn.
+      const int src0 = (2 * (q & 1)) << (two ? 4 : 3), src1 = (2 * (q & 1) + 1) << (two ? 4 : 3);
+      if (two) {
+        __syncwarp();  // the previous chunk's fragments are loaded
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          *reinterpret_cast<uint2*>(xw + (2 * i + m) * 128 + c0) = make_uint2(hi[i][0], hi[i][1]);
+          *reinterpret_cast<uint2*>(xw + (4 + 2 * i + m) * 128 + c0) = make_uint2(lo[i][0], lo[i][1]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float i0 = __shfl_sync(0xffffffffu, inv[i], src0 & 31);
+          const float i1 = __shfl_sync(0xffffffffu, inv[i], src1 & 31);
+          ef[c][i][0] = (q & 1) ? 0.f : i0;
+          ef[c][i][1] = (q & 1) ? 0.f : i1;
+          const uint8_t* row = xw + (g ^ (2 * i)) * 128 + 16 * q;
+          bfr[c][i][0] = ld_smem16(row);
+          bfr[c][i][1] = ld_smem16(row + 64);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          __syncwarp();
+          *reinterpret_cast<uint4*>(xw + m * 128 + c0) = make_uint4(hi[i][0], hi[i][1], hi[i][2], hi[i][3]);
+          *reinterpret_cast<uint4*>(xw + (4 + m) * 128 + c0) = make_uint4(lo[i][0], lo[i][1], lo[i][2], lo[i][3]);
+          // inverse prescales of x rows 0-3 from the lanes that computed them
+          ef[c][i][0] = __shfl_sync(0xffffffffu, inv[i], src0 & 31);
+          ef[c][i][1] = __shfl_sync(0xffffffffu, inv[i], src1 & 31);
+          __syncwarp();
+          bfr[c][i][0] = ld_smem16(xw + g * 128 + 16 * q);
+          bfr[c][i][1] = ld_smem16(xw + g * 128 + 64 + 16 * q);
+        }
+      }
+    }
   }
   named_bar(1, kWarps * 32);  // scales visible; every warp is done with its split buffer
 
   bool failed = false;
+  if (NCH == 1 && n_stages <= p.slots) {
+    // Every tile of the CTA sits in its own ring slot (one chunk of K; all copies were issued before
+    // griddepcontrol.wait): wait for all of them, issue every MMA of every tile, then scale and sum.
+    // The tensor-core results then arrive once for the whole CTA rather than once per tile.
+    bool ok = true;
+    for (int s = 0; s < n_stages; ++s) ok = ok && mbar_wait(&full[s], 0);
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
+    } else {
+      float d[kRingSlots][2][4];
+#pragma unroll
+      for (int t = 0; t < kRingSlots; ++t)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d[t][j][e] = 0.f;
+          const int kb = 2 * warp + j;
+          if (t < n_stages && kb < nkb) {
+            const uint8_t* rlo = smem + t * kStageBytes + g * kPitch + kb * 128 + 16 * q;
+            const uint8_t* rhi = rlo + 8 * kPitch;
+            const uint4 a0 = ld_smem16(rlo), a1 = ld_smem16(rlo + 64);
+            const uint4 h0 = ld_smem16(rhi), h1 = ld_smem16(rhi + 64);
+            const uint4 b0 = bfr[0][j][0], b1 = bfr[0][j][1];
+            mma_e4m3(d[t][j], a0.x, h0.x, a0.y, h0.y, b0.x, b0.y);
+            mma_e4m3(d[t][j], a0.z, h0.z, a0.w, h0.w, b0.z, b0.w);
+            mma_e4m3(d[t][j], a1.x, h1.x, a1.y, h1.y, b1.x, b1.y);
+            mma_e4m3(d[t][j], a1.z, h1.z, a1.w, h1.w, b1.z, b1.w);
+          }
+        }
+#pragma unroll
+      for (int t = 0; t < kRingSlots; ++t) {
+        if (t < n_stages) {
+          const int rl = min(t * kTileRows + g, R - 1), rh = min(t * kTileRows + g + 8, R - 1);
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int kb = 2 * warp + j;
+            if (kb < nkb) {
+              const float sl = sc[rl * nkb + kb], sh = sc[rh * nkb + kb];
+              acc[0] = fmaf(d[t][j][0], sl * ef[0][j][0], acc[0]);
+              acc[1] = fmaf(d[t][j][1], sl * ef[0][j][1], acc[1]);
+              acc[2] = fmaf(d[t][j][2], sh * ef[0][j][0], acc[2]);
+              acc[3] = fmaf(d[t][j][3], sh * ef[0][j][1], acc[3]);
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] += __shfl_xor_sync(0xffffffffu, acc[e], 2);
+          if (q < 2) {
+            float* rw = red + ((t * kWarps + warp) * kTileRows) * 4;
+            *reinterpret_cast<float2*>(rw + g * 4 + 2 * q) = make_float2(acc[0], acc[1]);
+            *reinterpret_cast<float2*>(rw + (g + 8) * 4 + 2 * q) = make_float2(acc[2], acc[3]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0)
+      for (int s = 0; s < n_stages; ++s) mbar_arrive(&empty[s]);
+  } else {
   for (int i = 0; i < n_stages; ++i) {
     const int slot = i % p.slots;
     if (!failed) {
@@ -283,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, NCH <= 2 ? 2 : 1) gemv_kernel(const 
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
+  }
   }
   named_bar(1, kWarps * 32);
   for (int i = tid; i < R * p.M; i += kWarps * 32) {
