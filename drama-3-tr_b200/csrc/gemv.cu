@@ -242,33 +242,42 @@ __global__ void __launch_bounds__(kThreads, NCH <= 2 ? 2 : 1) gemv_kernel(const 
   bool failed = false;
   if (NCH == 1 && n_stages <= p.slots) {
     // Every tile of the CTA sits in its own ring slot (one chunk of K; all copies were issued before
-    // griddepcontrol.wait): wait for all of them, issue every MMA of every tile, then scale and sum.
-    // The tensor-core results then arrive once for the whole CTA rather than once per tile.
+    // griddepcontrol.wait). Each tile's MMAs are issued as soon as its copy has landed and the sums
+    // of all tiles follow the last tile's MMAs: the tensor-core results then arrive once for the
+    // whole CTA rather than once per tile, and a tile that lands late still overlaps the MMAs of
+    // the tiles before it.
     bool ok = true;
-    for (int s = 0; s < n_stages; ++s) ok = ok && mbar_wait(&full[s], 0);
-    if (!__all_sync(0xffffffffu, ok)) {
-      if (lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
-    } else {
-      float d[kRingSlots][2][4];
+    float d[kRingSlots][2][4];
 #pragma unroll
-      for (int t = 0; t < kRingSlots; ++t)
+    for (int t = 0; t < kRingSlots; ++t) {
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) d[t][j][e] = 0.f;
-          const int kb = 2 * warp + j;
-          if (t < n_stages && kb < nkb) {
-            const uint8_t* rlo = smem + t * kStageBytes + g * kPitch + kb * 128 + 16 * q;
-            const uint8_t* rhi = rlo + 8 * kPitch;
-            const uint4 a0 = ld_smem16(rlo), a1 = ld_smem16(rlo + 64);
-            const uint4 h0 = ld_smem16(rhi), h1 = ld_smem16(rhi + 64);
-            const uint4 b0 = bfr[0][j][0], b1 = bfr[0][j][1];
-            mma_e4m3(d[t][j], a0.x, h0.x, a0.y, h0.y, b0.x, b0.y);
-            mma_e4m3(d[t][j], a0.z, h0.z, a0.w, h0.w, b0.z, b0.w);
-            mma_e4m3(d[t][j], a1.x, h1.x, a1.y, h1.y, b1.x, b1.y);
-            mma_e4m3(d[t][j], a1.z, h1.z, a1.w, h1.w, b1.z, b1.w);
+        for (int e = 0; e < 4; ++e) d[t][j][e] = 0.f;
+      if (t < n_stages && ok) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[t], 0));
+        if (ok) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int kb = 2 * warp + j;
+            if (kb < nkb) {
+              const uint8_t* rlo = smem + t * kStageBytes + g * kPitch + kb * 128 + 16 * q;
+              const uint8_t* rhi = rlo + 8 * kPitch;
+              const uint4 a0 = ld_smem16(rlo), a1 = ld_smem16(rlo + 64);
+              const uint4 h0 = ld_smem16(rhi), h1 = ld_smem16(rhi + 64);
+              const uint4 b0 = bfr[0][j][0], b1 = bfr[0][j][1];
+              mma_e4m3(d[t][j], a0.x, h0.x, a0.y, h0.y, b0.x, b0.y);
+              mma_e4m3(d[t][j], a0.z, h0.z, a0.w, h0.w, b0.z, b0.w);
+              mma_e4m3(d[t][j], a1.x, h1.x, a1.y, h1.y, b1.x, b1.y);
+              mma_e4m3(d[t][j], a1.z, h1.z, a1.w, h1.w, b1.z, b1.w);
+            }
           }
         }
+      }
+    }
+    if (!ok) {
+      if (lane == 0) atomicOr(&g_status, STATUS_TIMEOUT);
+    } else {
 #pragma unroll
       for (int t = 0; t < kRingSlots; ++t) {
         if (t < n_stages) {
