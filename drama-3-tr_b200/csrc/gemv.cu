@@ -14,6 +14,9 @@
 //   weight byte e4m3 -> f16 -> f32 on the CUDA cores and using packed fp32 FMAs measured 1.6x slower
 //   at 2048 x 4096: the conversions are low-throughput instructions.) Each K block's fp32 partial is
 //   scaled by its block scale, as the reference Triton kernel does (fp8_linear.py:21-26).
+// * When each of the CTA's 16-row tiles has its own ring slot, a tile's MMAs are issued as soon as
+//   its copy lands and the scaling and sums of all tiles follow the last tile's MMAs; otherwise the
+//   stages are consumed one at a time.
 // * The warps' partials of a row are added in a fixed order, so results do not depend on timing.
 // * A gathered row list (the audio head's rows of the full vocabulary matrix) only changes the
 //   source address of each row copy.
