@@ -14,9 +14,10 @@ from tests.helpers import REL_L2_TOL, rel_l2
 pytestmark = pytest.mark.gpu
 G = Path(__file__).resolve().parent / "golden"
 
-# (K, N) of the block-FP8 GEMV sweep, plus ragged / small cases
+# (K, N) of the block-FP8 GEMV sweep, plus ragged / small cases and (2048, 6144): three resident
+# 16-row tiles per CTA, the last one partly filled
 SHAPES = [(2048, 4096), (4096, 2048), (2048, 8192), (2048, 512), (2048, 4097), (512, 200), (8192, 128), (128, 1),
-          (384, 33)]
+          (384, 33), (2048, 6144)]
 
 
 def _case(k, n, seed, srows):
